@@ -1,0 +1,159 @@
+/*
+ * qmm.h -- C ABI of the B200 (sm_100a) MLX affine group-quantized linear.
+ *
+ * The operator is the one image-forger's `quant::Linear` implements
+ * (src/quant.rs): a weight matrix W [n, k] stored as `bits`-wide unsigned
+ * codes packed little-end-first into uint32 words along k (first code in the
+ * lowest bits), one bf16 scale and one bf16 offset ("biases" in MLX naming)
+ * per group of `group` consecutive k, w = scale * q + offset, and an optional
+ * per-output additive bias.  y [m, n] = x [m, k] . W^T (+ bias).
+ *
+ * Conventions of every entry point:
+ *   - plain pointers to device memory, element counts as int64_t, the CUDA
+ *     stream as an opaque `void *` (a cudaStream_t; NULL = legacy stream);
+ *   - nothing is allocated; outputs are written into caller buffers;
+ *   - launches are asynchronous on the given stream;
+ *   - the return value is a qmm_status; the message of the last failure on the
+ *     calling thread is available from qmm_last_error();
+ *   - bf16 tensors are passed as uint16_t (raw bf16 bits), row-major and
+ *     contiguous.
+ * There is no CPU implementation behind this header: a process without a
+ * usable CUDA device gets QMM_ERR_CUDA.
+ */
+#ifndef QMM_H
+#define QMM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QMM_API __attribute__((visibility("default")))
+#else
+#define QMM_API
+#endif
+
+/* Status codes.  Replaces the `candle_core::Error` results of quant.rs. */
+typedef enum qmm_status {
+    QMM_OK = 0,
+    QMM_ERR_INVALID_ARGUMENT = 1, /* null pointer where one is required, bad enum */
+    QMM_ERR_BAD_SHAPE = 2,        /* shapes inconsistent (quant.rs:50-67, 438-445, 506-513) */
+    QMM_ERR_UNSUPPORTED = 3,      /* valid layout the fused kernels do not cover: the caller
+                                     dequantizes and runs a dense GEMM (quant.rs:121, 783-790) */
+    QMM_ERR_MISALIGNED = 4,       /* a pointer is not 16-byte aligned */
+    QMM_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
+    QMM_ERR_TIMEOUT = 6           /* a bounded device-side wait expired (see qmm_device_error) */
+} qmm_status;
+
+/* Element type of qmm_dequantize's output (quant.rs:570-575: bf16 or f32). */
+typedef enum qmm_dtype {
+    QMM_DTYPE_BF16 = 0,
+    QMM_DTYPE_F32 = 1
+} qmm_dtype;
+
+/*
+ * A packed quantized weight: the `Affine` state of quant.rs:31-39.
+ *   packed : uint32 [n, k * bits / 32]   (MLX "weight")
+ *   scales : bf16   [n, k / group]       (MLX "scales")
+ *   biases : bf16   [n, k / group]       (MLX "biases", quant.rs `offsets`)
+ * The struct only borrows the pointers; weights are never modified.
+ */
+typedef struct qmm_weight {
+    const uint32_t *packed;
+    const uint16_t *scales;
+    const uint16_t *biases;
+    int64_t n;      /* output features (rows of W) */
+    int64_t k;      /* input features */
+    int32_t bits;   /* 2, 4 or 8 */
+    int32_t group;  /* inputs per scale/offset group */
+} qmm_weight;
+
+/* Activation applied in the fused epilogue. */
+typedef enum qmm_activation {
+    QMM_ACT_NONE = 0,
+    QMM_ACT_GELU_TANH = 1,   /* 0.5 t (1 + tanh(sqrt(2/pi) (t + 0.044715 t^3))) */
+    QMM_ACT_SILU = 2         /* t / (1 + exp(-t)) */
+} qmm_activation;
+
+/*
+ * Fused epilogue, evaluated in f32 on the accumulator before one rounding to
+ * bf16:  y = residual + gate * act(acc + bias).
+ * Every pointer may be NULL (term omitted).  bias and gate are bf16 [n]
+ * (quant.rs:157-160 adds `bias`; src/dit.rs:88-93 multiplies by a per-feature
+ * gate and adds the residual stream); residual is bf16 [m, n] and may alias y.
+ */
+typedef struct qmm_epilogue {
+    const uint16_t *bias;
+    const uint16_t *gate;
+    const uint16_t *residual;
+    int32_t activation;     /* qmm_activation */
+} qmm_epilogue;
+
+/* Kernel selection for qmm_linear_ex (tests and benchmarks). */
+typedef enum qmm_path {
+    QMM_PATH_AUTO = 0,   /* m <= 16: GEMV, otherwise the tcgen05 GEMM */
+    QMM_PATH_GEMV = 1,   /* warp-per-row streaming kernel, any m (slow for large m) */
+    QMM_PATH_GEMM = 2    /* tcgen05/TMEM GEMM, any m >= 1 */
+} qmm_path;
+
+/* ABI version of the loaded library (QMM_ABI_VERSION at build time). */
+QMM_API int32_t qmm_abi_version(void);
+
+/* Message of the last non-OK status returned on the calling thread ("" if none). */
+QMM_API const char *qmm_last_error(void);
+
+/*
+ * Infers bits and group from tensor shapes exactly as `Linear::load` does
+ * (quant.rs:43-77): scales [scales_rows, scales_cols] must be [output, groups]
+ * with groups > 0 dividing input; packed [packed_rows, packed_words] must have
+ * packed_rows == output and packed_words * 32 == bits * input for bits in
+ * {2, 4, 8}.  Host-only; touches no device memory.
+ */
+QMM_API qmm_status qmm_infer_layout(int64_t input, int64_t output,
+                            int64_t scales_rows, int64_t scales_cols,
+                            int64_t packed_rows, int64_t packed_words,
+                            int32_t *bits_out, int32_t *group_out);
+
+/* Checks a qmm_weight for internal consistency (host-only, no device access). */
+QMM_API qmm_status qmm_validate(const qmm_weight *w);
+
+/*
+ * Dense W [n, k] = T(f32(scale) * q + f32(offset)), T = bf16 (round to
+ * nearest even) or f32.  Bit-exact with `Dequantize::cpu_fwd`
+ * (quant.rs:528-577) and the Metal `dequantize` kernel (quant.rs:186-206).
+ * Replaces CustomOp3 "mlx-dequantize" (quant.rs:523-643).
+ */
+QMM_API qmm_status qmm_dequantize(const qmm_weight *w, void *dst, int32_t dtype, void *stream);
+
+/*
+ * y [m, n] = epilogue(x [m, k] . W^T).  Replaces CustomOp2 "mlx-qmm"
+ * (quant.rs:411-503) plus the bias add of `Affine::forward` (quant.rs:157-160).
+ * x, y, residual: 16-byte aligned; y must not overlap x.  m == 0 is a no-op.
+ * ep may be NULL (no bias, no gate, no residual, no activation).
+ */
+QMM_API qmm_status qmm_linear(const qmm_weight *w, const uint16_t *x, int64_t m,
+                      const qmm_epilogue *ep, uint16_t *y, void *stream);
+
+/* qmm_linear with an explicit kernel choice (qmm_path). */
+QMM_API qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
+                         const qmm_epilogue *ep, uint16_t *y, int32_t path,
+                         void *stream);
+
+/*
+ * Reads and clears the device-side error word that bounded waits inside the
+ * GEMM set when they expire (0 = none).  Synchronizes `stream`.
+ */
+QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
+
+/* Number of kernels this library has launched in the calling process. */
+QMM_API uint64_t qmm_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMM_H */

@@ -1,0 +1,210 @@
+// C ABI of libqmm (include/qmm.h): argument validation, kernel dispatch,
+// error reporting.
+//
+// Validation mirrors image-forger's `Linear::load` (src/quant.rs:43-77) and
+// the shape checks of its Qmm/Dequantize custom ops (src/quant.rs:438-451,
+// 505-513, 589-598).  Dispatch mirrors `Module::forward` (src/quant.rs:115-124):
+// layouts the fused kernels cover run fused; anything else returns
+// QMM_ERR_UNSUPPORTED so the caller dequantizes and runs a dense GEMM, the way
+// the reference falls back to `self.dense()?.forward(x)` (src/quant.rs:121).
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "qmm_internal.h"
+
+namespace qmm {
+
+// The device-side error word that bounded waits write (see qmm_common.cuh).
+__device__ uint32_t g_device_error = 0;
+
+namespace {
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {};
+uint32_t *g_err_addr[kMaxDevices] = {};
+std::mutex g_dev_mutex;
+
+int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    return dev;
+}
+}  // namespace
+
+qmm_status fail(qmm_status status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return status;
+}
+
+qmm_status cuda_fail(cudaError_t e, const char *what) {
+    return fail(QMM_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+uint32_t *device_error_word() {
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!g_err_addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess)
+            g_err_addr[dev] = static_cast<uint32_t *>(p);
+    }
+    return g_err_addr[dev];
+}
+
+int sm_count() {
+    const int dev = current_device();
+    if (g_sm_count[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        g_sm_count[dev] = n;
+    }
+    return g_sm_count[dev];
+}
+
+void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+}  // namespace qmm
+
+using qmm::fail;
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static qmm_status check_device() {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return qmm::cuda_fail(e, "no CUDA device");
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (major != 10) return fail(QMM_ERR_CUDA, "device %d is not sm_100 (compute capability %d.x)", dev, major);
+    return QMM_OK;
+}
+
+extern "C" {
+
+int32_t qmm_abi_version(void) { return QMM_ABI_VERSION; }
+
+const char *qmm_last_error(void) { return qmm::t_last_error.c_str(); }
+
+uint64_t qmm_launch_count(void) { return qmm::g_launches.load(std::memory_order_relaxed); }
+
+qmm_status qmm_infer_layout(int64_t input, int64_t output, int64_t scales_rows,
+                            int64_t scales_cols, int64_t packed_rows, int64_t packed_words,
+                            int32_t *bits_out, int32_t *group_out) {
+    if (!bits_out || !group_out) return fail(QMM_ERR_INVALID_ARGUMENT, "null output pointer");
+    if (input <= 0 || output <= 0)
+        return fail(QMM_ERR_BAD_SHAPE, "a %lld->%lld linear has no weights", (long long)input,
+                    (long long)output);
+    const int64_t groups = scales_cols;
+    if (scales_rows != output || groups <= 0 || input % groups != 0)
+        return fail(QMM_ERR_BAD_SHAPE, "scales [%lld, %lld] do not match a %lld->%lld linear",
+                    (long long)scales_rows, (long long)scales_cols, (long long)input,
+                    (long long)output);
+    const int64_t bits = packed_words * 32 / input;
+    if (packed_rows != output || packed_words * 32 != bits * input ||
+        !(bits == 2 || bits == 4 || bits == 8))
+        return fail(QMM_ERR_BAD_SHAPE,
+                    "packed weight [%lld, %lld] is not 2-, 4- or 8-bit for %lld inputs",
+                    (long long)packed_rows, (long long)packed_words, (long long)input);
+    *bits_out = (int32_t)bits;
+    *group_out = (int32_t)(input / groups);
+    return QMM_OK;
+}
+
+qmm_status qmm_validate(const qmm_weight *w) {
+    if (!w) return fail(QMM_ERR_INVALID_ARGUMENT, "null weight");
+    if (!w->packed || !w->scales || !w->biases)
+        return fail(QMM_ERR_INVALID_ARGUMENT, "weight has a null packed/scales/biases pointer");
+    if (w->n <= 0 || w->k <= 0) return fail(QMM_ERR_BAD_SHAPE, "weight is %lldx%lld", (long long)w->n, (long long)w->k);
+    if (!(w->bits == 2 || w->bits == 4 || w->bits == 8))
+        return fail(QMM_ERR_BAD_SHAPE, "%d-bit codes are not 2-, 4- or 8-bit", w->bits);
+    if (w->group <= 0 || w->k % w->group != 0)
+        return fail(QMM_ERR_BAD_SHAPE, "group %d does not divide %lld inputs", w->group, (long long)w->k);
+    if ((w->k * w->bits) % 32 != 0)
+        return fail(QMM_ERR_BAD_SHAPE, "%lld %d-bit codes do not fill whole words", (long long)w->k, w->bits);
+    if (!aligned16(w->packed))
+        return fail(QMM_ERR_MISALIGNED, "packed weights are not 16-byte aligned");
+    return QMM_OK;
+}
+
+qmm_status qmm_dequantize(const qmm_weight *w, void *dst, int32_t dtype, void *stream) {
+    qmm_status s = qmm_validate(w);
+    if (s != QMM_OK) return s;
+    if (!dst) return fail(QMM_ERR_INVALID_ARGUMENT, "null destination");
+    if (dtype != QMM_DTYPE_BF16 && dtype != QMM_DTYPE_F32)
+        return fail(QMM_ERR_INVALID_ARGUMENT, "dequantize does not support dtype %d", dtype);
+    if (!aligned16(dst)) return fail(QMM_ERR_MISALIGNED, "destination is not 16-byte aligned");
+    if ((s = check_device()) != QMM_OK) return s;
+    return qmm::launch_dequantize(*w, dst, dtype, static_cast<cudaStream_t>(stream));
+}
+
+qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
+                         const qmm_epilogue *ep, uint16_t *y, int32_t path, void *stream) {
+    qmm_status s = qmm_validate(w);
+    if (s != QMM_OK) return s;
+    if (m < 0) return fail(QMM_ERR_BAD_SHAPE, "negative token count %lld", (long long)m);
+    if (m == 0) return QMM_OK;
+    if (!x || !y) return fail(QMM_ERR_INVALID_ARGUMENT, "null x or y");
+    if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM)
+        return fail(QMM_ERR_INVALID_ARGUMENT, "unknown path %d", path);
+    qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
+    if (e.activation < QMM_ACT_NONE || e.activation > QMM_ACT_SILU)
+        return fail(QMM_ERR_INVALID_ARGUMENT, "unknown activation %d", e.activation);
+    if (!aligned16(x) || !aligned16(y) || (e.residual && !aligned16(e.residual)))
+        return fail(QMM_ERR_MISALIGNED, "x, y and residual must be 16-byte aligned");
+    {
+        const uintptr_t xb = reinterpret_cast<uintptr_t>(x), yb = reinterpret_cast<uintptr_t>(y);
+        const uintptr_t xe = xb + (uintptr_t)(m * w->k * 2), ye = yb + (uintptr_t)(m * w->n * 2);
+        if (xb < ye && yb < xe) return fail(QMM_ERR_INVALID_ARGUMENT, "y overlaps x");
+    }
+    if ((s = check_device()) != QMM_OK) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (path == QMM_PATH_AUTO) path = (m <= 16 && qmm::gemv_supported(*w, m)) ? QMM_PATH_GEMV : QMM_PATH_GEMM;
+    if (path == QMM_PATH_GEMV) {
+        if (!qmm::gemv_supported(*w, m))
+            return fail(QMM_ERR_UNSUPPORTED,
+                        "gemv: %d-bit, group %d, k=%lld, m=%lld is outside the kernel's layouts",
+                        w->bits, w->group, (long long)w->k, (long long)m);
+        return qmm::launch_gemv(*w, x, m, e, y, st);
+    }
+    if (!qmm::gemm_supported(*w))
+        return fail(QMM_ERR_UNSUPPORTED,
+                    "gemm: %d-bit, group %d, k=%lld is outside the kernel's layouts (needs 4/8-bit, "
+                    "k %% 64 == 0, group 32 or a multiple of 64)",
+                    w->bits, w->group, (long long)w->k);
+    return qmm::launch_gemm(*w, x, m, e, y, st);
+}
+
+qmm_status qmm_linear(const qmm_weight *w, const uint16_t *x, int64_t m, const qmm_epilogue *ep,
+                      uint16_t *y, void *stream) {
+    return qmm_linear_ex(w, x, m, ep, y, QMM_PATH_AUTO, stream);
+}
+
+qmm_status qmm_device_error(void *stream, uint32_t *code_out) {
+    if (!code_out) return fail(QMM_ERR_INVALID_ARGUMENT, "null output pointer");
+    qmm_status s = check_device();
+    if (s != QMM_OK) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return qmm::cuda_fail(e, "stream synchronize");
+    uint32_t v = 0, zero = 0;
+    e = cudaMemcpyFromSymbol(&v, qmm::g_device_error, sizeof v);
+    if (e != cudaSuccess) return qmm::cuda_fail(e, "read device error word");
+    if (v != 0) {
+        e = cudaMemcpyToSymbol(qmm::g_device_error, &zero, sizeof zero);
+        if (e != cudaSuccess) return qmm::cuda_fail(e, "clear device error word");
+    }
+    *code_out = v;
+    return v == 0 ? QMM_OK : fail(QMM_ERR_TIMEOUT, "device-side wait expired (code %u)", v);
+}
+
+}  // extern "C"

@@ -1,0 +1,55 @@
+// Fused epilogue: y = residual + gate * act(acc + bias), f32, one bf16 rounding.
+// The reference applies these as separate bf16 tensor ops after the linear
+// (image-forger src/quant.rs:157-160 bias; src/dit.rs:88-93 gate and residual).
+#pragma once
+
+#include "qmm_common.cuh"
+
+namespace qmm {
+
+__device__ __forceinline__ float apply_activation(float t, int act) {
+    if (act == 1) {  // GELU, tanh approximation
+        const float c = 0.7978845608028654f;
+        return 0.5f * t * (1.0f + tanhf(c * (t + 0.044715f * t * t * t)));
+    }
+    if (act == 2) return t / (1.0f + expf(-t));  // SiLU
+    return t;
+}
+
+struct EpilogueArgs {
+    const uint16_t *bias;      // [n] or null
+    const uint16_t *gate;      // [n] or null
+    const uint16_t *residual;  // [m, n] or null
+    int32_t act;
+};
+
+// Per-output-feature constants of the epilogue.
+struct FeatureConsts {
+    float bias;
+    float gate;
+};
+
+__device__ __forceinline__ FeatureConsts load_feature_consts(const EpilogueArgs &e, int64_t n,
+                                                             bool valid) {
+    FeatureConsts c{0.0f, 1.0f};
+    if (valid) {
+        if (e.bias) c.bias = bf16_bits_to_f32(__ldg(e.bias + n));
+        if (e.gate) c.gate = bf16_bits_to_f32(__ldg(e.gate + n));
+    }
+    return c;
+}
+
+__device__ __forceinline__ float epilogue_value(const EpilogueArgs &e, const FeatureConsts &c,
+                                                float acc, const uint16_t *residual_elem) {
+    float t = apply_activation(acc + c.bias, e.act);
+    if (e.gate) t = t * c.gate;
+    if (residual_elem) t = bf16_bits_to_f32(*residual_elem) + t;
+    return t;
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
+    __nv_bfloat16 b = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t *>(&b);
+}
+
+}  // namespace qmm

@@ -1,0 +1,39 @@
+// Host-side internals shared by the translation units of libqmm.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qmm.h"
+
+namespace qmm {
+
+// Records a failure message for qmm_last_error() and returns `status`.
+qmm_status fail(qmm_status status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// Converts a CUDA runtime error into QMM_ERR_CUDA with a message.
+qmm_status cuda_fail(cudaError_t e, const char *what);
+
+// Device address of the library's device error word on the current device.
+uint32_t *device_error_word();
+
+// Streaming multiprocessors of the current device.
+int sm_count();
+
+// Counts kernel launches (exported through qmm_launch_count()).
+void count_launch(uint64_t n = 1);
+
+// Launchers.  Arguments are validated by the caller (qmm_api.cu).
+qmm_status launch_dequantize(const qmm_weight &w, void *dst, int32_t dtype, cudaStream_t st);
+
+// True when the GEMV kernel supports this layout and token count.
+bool gemv_supported(const qmm_weight &w, int64_t m);
+qmm_status launch_gemv(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
+                       uint16_t *y, cudaStream_t st);
+
+// True when the tcgen05 GEMM supports this layout.
+bool gemm_supported(const qmm_weight &w);
+qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
+                       uint16_t *y, cudaStream_t st);
+
+}  // namespace qmm

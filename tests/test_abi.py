@@ -1,0 +1,89 @@
+"""The C-ABI library builds for sm_100a, loads, and exports every symbol that
+include/qmm.h declares; host-only entry points validate like `Linear::load`
+(src/quant.rs:43-77).  No compute calls: this file needs no GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from qwen_imager_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "qmm.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^QMM_API\s+(?:const\s+)?\w+\s+\*?\s*(qmm_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_binding_table():
+    assert declared_symbols() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.qmm_abi_version() == 1
+
+
+def test_library_is_built_for_sm100a_only():
+    import subprocess
+    out = subprocess.run(["cuobjdump", "--list-elf", _lib.library_path()], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert arches == {"100a"}, arches
+
+
+@pytest.mark.parametrize("input,output,scales,packed,expect", [
+    (192, 96, (96, 3), (96, 24), (4, 64)),
+    (192, 96, (96, 3), (96, 48), (8, 64)),
+    (4096, 1024, (1024, 128), (1024, 256), (2, 32)),
+    (3072, 18432, (18432, 48), (18432, 384), (4, 64)),
+])
+def test_infer_layout_accepts_mlx_packs(input, output, scales, packed, expect):
+    assert _lib.infer_layout(input, output, scales, packed) == expect
+
+
+@pytest.mark.parametrize("input,output,scales,packed", [
+    (128, 96, (96, 3), (96, 24)),   # groups do not divide the input
+    (192, 96, (96, 3), (96, 20)),   # truncated packing (reference test, src/quant.rs:804-806)
+    (192, 96, (95, 3), (96, 24)),   # scales rows
+    (192, 96, (96, 0), (96, 24)),   # no groups
+    (192, 96, (96, 3), (96, 18)),   # 3-bit
+    (192, 96, (96, 3), (96, 96)),   # 16-bit
+])
+def test_infer_layout_rejects_bad_packing(input, output, scales, packed):
+    with pytest.raises(_lib.QmmError) as e:
+        _lib.infer_layout(input, output, scales, packed)
+    assert e.value.status == _lib.QMM_ERR_BAD_SHAPE
+
+
+def test_validate_rejects_null_and_misaligned_weights():
+    lib = _lib.load()
+    w = _lib.QmmWeight(None, None, None, 96, 192, 4, 64)
+    assert lib.qmm_validate(ctypes.byref(w)) == _lib.QMM_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.qmm_last_error()
+    w = _lib.QmmWeight(0x1008, 0x2000, 0x3000, 96, 192, 4, 64)
+    assert lib.qmm_validate(ctypes.byref(w)) == _lib.QMM_ERR_MISALIGNED
+    w = _lib.QmmWeight(0x1000, 0x2000, 0x3000, 96, 192, 3, 64)
+    assert lib.qmm_validate(ctypes.byref(w)) == _lib.QMM_ERR_BAD_SHAPE
+    w = _lib.QmmWeight(0x1000, 0x2000, 0x3000, 96, 192, 4, 50)
+    assert lib.qmm_validate(ctypes.byref(w)) == _lib.QMM_ERR_BAD_SHAPE
+    w = _lib.QmmWeight(0x1000, 0x2000, 0x3000, 96, 192, 4, 64)
+    assert lib.qmm_validate(ctypes.byref(w)) == _lib.QMM_OK
+    assert lib.qmm_validate(None) == _lib.QMM_ERR_INVALID_ARGUMENT
+
+
+def test_compute_entry_points_fail_loudly_without_a_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    lib = _lib.load()
+    w = _lib.QmmWeight(0x1000, 0x2000, 0x3000, 96, 192, 4, 64)
+    st = lib.qmm_linear(ctypes.byref(w), 0x4000, 5, None, 0x8000, None)
+    assert st == _lib.QMM_ERR_CUDA
+    st = lib.qmm_dequantize(ctypes.byref(w), 0x8000, 0, None)
+    assert st == _lib.QMM_ERR_CUDA
