@@ -56,3 +56,15 @@ def bf16_ulp_diff(a_bf16, b_bf16):
         u = u.astype(np.int32)
         return np.where(u & 0x8000, -(u & 0x7FFF), u)
     return np.abs(ordered(a_bf16) - ordered(b_bf16))
+
+
+def assert_one_rounding(got, ref_f32, oracle=O):
+    """Within 1 bf16 ulp of the f32 reference, except where f32 accumulation
+    order dominates (outputs near zero): there |d| <= 2^-12 max|ref|."""
+    ref = oracle.f32_to_bf16(ref_f32)
+    ulps = bf16_ulp_diff(got, ref)
+    d = np.abs(oracle.bf16_to_f32(got).astype(np.float64) - np.asarray(ref_f32, dtype=np.float64))
+    tol = np.abs(ref_f32).max() * 2.0**-12
+    bad = (ulps > 1) & (d > tol)
+    assert not bad.any(), (int(ulps.max()), float(d[bad].max() / np.abs(ref_f32).max()))
+    assert (ulps > 0).mean() < 0.05
