@@ -1,0 +1,407 @@
+"""Benchmark of the MLX affine quantized linear on B200 (one JSON line).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload ffn_up|linear_4bit|ffn_down|adaln_gemv]
+
+Default workload (`ffn_up`, the configuration the headline metric is quoted
+on): the DiT FFN up projection, x bf16 [4352, 3072] ~ N(0,1) times 8-bit
+group-64 weights [12288, 3072] (W ~ N(0, 0.02), MLX affine quantization),
+plus the adaLN modulation GEMV of the same configuration, x [1, 3072] =
+SiLU(N(0,1)) times 4-bit weights [18432, 3072].  One step runs both linears
+once.  Data is synthetic and seeded; three weight/input sets (~290 MB, more
+than the 126 MB L2) rotate across steps so every step streams from HBM.
+
+With N > 1 (torchrun, one process per GPU) every rank runs its own batch of
+the same workload (weak scaling: tokens are independent, no data-path
+collective); value is the total over ranks, timed as the max over ranks.
+
+--impl reference times the reference's CPU path for the same workload on the
+host cores (the oracle's restatement: per-call f32 dequantization plus an f32
+GEMM), on a bounded row sample, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (description, [(m, k, n, bits, extras)], seed)
+    "ffn_up": ("FFN up 8-bit [4352x3072]x[12288x3072]^T + adaLN GEMV 4-bit [1x3072]x[18432x3072]^T",
+               [(4352, 3072, 12288, 8, {}), (1, 3072, 18432, 4, {"silu_input": True})], 1),
+    "linear_4bit": ("4-bit linear [4096x3072]x[3072x3072]^T + bias",
+                    [(4096, 3072, 3072, 4, {"bias": True})], 0),
+    "ffn_down": ("FFN down 4-bit [4352x12288]x[3072x12288]^T + fused residual, GELU-tanh input",
+                 [(4352, 12288, 3072, 4, {"residual": True, "gelu_input": True})], 2),
+    "adaln_gemv": ("adaLN GEMV 4-bit [1x3072]x[18432x3072]^T", [(1, 3072, 18432, 4, {"silu_input": True})], 1),
+}
+ROTATE = 3
+METRIC = "qmm TFLOP/s (quantized DiT linears, bf16 tensor cores)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="ffn_up")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return p.parse_args()
+
+
+def step_flops(layers):
+    return sum(2.0 * m * n * k for (m, k, n, _b, _e) in layers)
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic(workload):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"traffic_{workload}.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons through NVML during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                mask = get_reasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.02)
+
+    def __enter__(self):
+        if self.nv:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------- our arm
+def build_sets(layers, seed, device):
+    import torch
+
+    from qwen_imager_b200.synthetic import gaussian, quantized_linear
+
+    sets = []
+    for r in range(ROTATE):
+        entry = []
+        for li, (m, k, n, bits, ex) in enumerate(layers):
+            s = seed * 1000 + r * 10 + li
+            lin = quantized_linear(n, k, bits, seed=s, bias_std=0.01 if ex.get("bias") else None, device=device)
+            g = torch.Generator(device=device)
+            g.manual_seed(s + 500)
+            x = gaussian((m, k), 1.0, g, device)
+            if ex.get("silu_input"):
+                x = torch.nn.functional.silu(x)
+            if ex.get("gelu_input"):
+                x = torch.nn.functional.gelu(x, approximate="tanh")
+            x = x.to(torch.bfloat16)
+            res = gaussian((m, n), 1.0, g, device).to(torch.bfloat16) if ex.get("residual") else None
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+            entry.append((lin, x, res, y))
+        sets.append(entry)
+    return sets
+
+
+def run_ours(args, rank, world, device):
+    import torch
+
+    from qwen_imager_b200 import _lib, device_error
+
+    desc, layers, seed = WORKLOADS[args.workload]
+    sets = build_sets(layers, seed + 17 * rank, device)
+    dist = world > 1
+    if dist:
+        import torch.distributed as tdist
+
+    def step(i, ev=None):
+        for li, (lin, x, res, y) in enumerate(sets[i % ROTATE]):
+            if ev is not None:
+                ev[li][0].record()
+            lin.forward_fused(x, residual=res, out=y)
+            if ev is not None:
+                ev[li][1].record()
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    if device_error(device):
+        raise RuntimeError("device-side wait expired during warm-up")
+
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in layers]
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device())
+    if dist:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    with sampler:
+        t0.record()
+        for i in range(args.steps):
+            step(i, evs[i])
+        t1.record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    if dist:
+        tdist.barrier()
+    elapsed = t0.elapsed_time(t1)
+    kernel_ms = [sum(e[li][0].elapsed_time(e[li][1]) for e in evs) / args.steps for li in range(len(layers))]
+    if dist:
+        t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    ms_per_step = elapsed / args.steps
+    flops = step_flops(layers)
+    value = world * flops / (ms_per_step * 1e-3) / 1e12
+
+    # End to end through the public API with host buffers: per step, copy the
+    # step's inputs from pinned host memory, run, read the outputs back.
+    e2e = None
+    if not args.no_e2e:
+        host = []
+        for (lin, x, res, y) in sets[0]:
+            hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            hx.copy_(x)
+            hr = None
+            if res is not None:
+                hr = torch.empty(res.shape, dtype=res.dtype, pin_memory=True)
+                hr.copy_(res)
+            hy = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+            host.append((hx, hr, hy))
+        h2d = sum(hx.numel() * 2 + (hr.numel() * 2 if hr is not None else 0) for hx, hr, _ in host)
+        d2h = sum(hy.numel() * 2 for _, _, hy in host)
+
+        def e2e_step(i):
+            for (lin, x, res, y), (hx, hr, hy) in zip(sets[i % ROTATE], host):
+                x.copy_(hx, non_blocking=True)
+                if hr is not None:
+                    res.copy_(hr, non_blocking=True)
+                lin.forward_fused(x, residual=res, out=y)
+                hy.copy_(y, non_blocking=True)
+
+        for i in range(2):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        if dist:
+            tdist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        n_e2e = max(3, min(args.steps, 20))
+        for i in range(n_e2e):
+            e2e_step(i)
+        b.record()
+        torch.cuda.synchronize()
+        e_ms = a.elapsed_time(b) / n_e2e
+        if dist:
+            t = torch.tensor([e_ms], device=device, dtype=torch.float64)
+            tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": round(world * flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    if device_error(device):
+        raise RuntimeError("device-side wait expired during the timed region")
+
+    # Roofline of the dominant kernel (largest FLOP count).
+    dom = max(range(len(layers)), key=lambda li: 2.0 * layers[li][0] * layers[li][1] * layers[li][2])
+    m, k, n, bits, _ = layers[dom]
+    peak_tf, hbm_gbs, peak_kind = measured_peaks()
+    if m <= 16:
+        alg_bytes = n * k * bits / 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
+        achieved = alg_bytes / (kernel_ms[dom] * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
+                "frac": round(achieved / hbm_gbs, 4)}
+    else:
+        achieved = 2.0 * m * n * k / (kernel_ms[dom] * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                "frac": round(achieved / peak_tf, 4)}
+    roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback"
+    roof["traffic"] = profile_traffic(args.workload)
+    roof["kernel_ms"] = round(kernel_ms[dom], 5)
+    per_layer = []
+    for li, (m, k, n, bits, _) in enumerate(layers):
+        entry = {"m": m, "k": k, "n": n, "bits": bits, "kernel_us": round(kernel_ms[li] * 1e3, 2)}
+        if m <= 16:
+            b = n * k * bits / 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
+            entry["GB/s"] = round(b / (kernel_ms[li] * 1e-3) / 1e9, 1)
+            entry["hbm_frac"] = round(entry["GB/s"] / hbm_gbs, 4)
+        else:
+            entry["TFLOP/s"] = round(2.0 * m * n * k / (kernel_ms[li] * 1e-3) / 1e12, 1)
+        per_layer.append(entry)
+    return {
+        "value": round(value, 3), "ms_per_step": round(ms_per_step, 5), "e2e": e2e, "roofline": roof,
+        "gpu_launches": int(launches), "layers": per_layer, "clocks": sampler.summary(),
+    }
+
+
+# --------------------------------------------------------------------- CPU arm
+CPU_SAMPLE_ROWS = 128
+
+
+def cpu_reference(layers, seed, steps, warmup):
+    """Times the reference CPU path (oracle restatement) for one step of the
+    workload: full per-call dequantization of every weight plus the f32 GEMM on
+    a CPU_SAMPLE_ROWS-row sample of x, extrapolated linearly in rows."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    O.build()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    O.lib().oracle_set_threads(threads)
+    rng = np.random.default_rng(seed)
+    data = []
+    for (m, k, n, bits, ex) in layers:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+        packed, scales, biases = O.quantize_affine(w, bits, 64)
+        rows = min(m, CPU_SAMPLE_ROWS)
+        x = O.f32_to_bf16(rng.standard_normal((rows, k), dtype=np.float32))
+        data.append((m, rows, packed, scales, biases, bits, x))
+    times = []
+    for it in range(warmup + steps):
+        t_step = 0.0
+        for (m, rows, packed, scales, biases, bits, x) in data:
+            t0 = time.perf_counter()
+            wf = O.dequantize_f32(packed, scales, biases, bits, 64)
+            t1 = time.perf_counter()
+            y = torch.from_numpy(O.bf16_to_f32(x)) @ torch.from_numpy(wf).T
+            O.f32_to_bf16(y.numpy())
+            t2 = time.perf_counter()
+            t_step += (t1 - t0) + (t2 - t1) * (m / rows)
+        if it >= warmup:
+            times.append(t_step)
+    t = statistics.median(times)
+    sample = (f"per step: every weight dequantized to f32 in full (as the reference does per call), "
+              f"f32 GEMM on {min(CPU_SAMPLE_ROWS, max(l[0] for l in layers))} of the token rows, GEMM time "
+              f"scaled linearly to all rows; median of {steps} steps")
+    return step_flops(layers) / t / 1e12, t, threads, sample
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    desc, layers, seed = WORKLOADS[args.workload]
+    config = {"workload": f"{args.workload}: {desc}", "global_batch": world,
+              "tokens_per_rank": max(l[0] for l in layers), "group": 64,
+              "parallelism": f"dp{world} (independent token batches)",
+              "l2": f"{ROTATE} rotating weight/input sets larger than L2 (no flush)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        value, t, cores, sample = cpu_reference(layers, seed, args.steps, args.warmup)
+        out = {"metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "impl": "reference",
+               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+               "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                "sample": sample},
+               "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": 0}}
+        print(json.dumps(out), flush=True)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    try:
+        res = run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            import torch.distributed as tdist
+            tdist.barrier()
+    out = {"metric": METRIC, "value": res["value"], "unit": "TFLOP/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded random weights, MLX affine quantized; random activations)",
+           "config": config, "e2e": res["e2e"], "roofline": res["roofline"],
+           "gpu_launches": res["gpu_launches"], "clocks": res["clocks"], "layers": res["layers"]}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            value, t, cores, sample = cpu_reference(layers, seed, 3, 1)
+            out["cpu_baseline"] = {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores,
+                                   "kind": "port", "sample": sample}
+        except Exception as exc:  # the CPU leg must not hide the GPU result
+            out["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -54,6 +54,8 @@ def lib() -> ctypes.CDLL:
             l.oracle_epilogue_bf16.argtypes = [_f32p, _u16p, _u16p, _i32, _i64, _i64, _u16p]
             l.oracle_bf16_from_f32_array.argtypes = [_f32p, _u16p, _i64]
             l.oracle_f32_from_bf16_array.argtypes = [_u16p, _f32p, _i64]
+            l.oracle_set_threads.argtypes = [_i32]
+            l.oracle_get_threads.restype = _i32
             _lib = l
     return _lib
 
@@ -181,3 +183,23 @@ def quantize_affine(w_f32: np.ndarray, bits: int, group: int = 64):
     shifts = (np.arange(per_word, dtype=np.uint32) * bits)[None, None, :]
     packed = np.bitwise_or.reduce(q << shifts, axis=2).astype(np.uint32)
     return packed, scale_b, bias_b
+
+
+def reference_forward_cpu(x_bf16, packed, scales, biases, bits: int, group: int, bias=None,
+                          threads: int = 0) -> np.ndarray:
+    """The reference's CPU forward as it runs per call (src/quant.rs:105-113, 119):
+    re-dequantize W to f32 (row-parallel, like rayon's par_chunks_mut), x to f32,
+    f32 GEMM plus f32 bias, cast to bf16.  The f32 GEMM of Candle's third-party
+    `gemm` crate is stood in for by torch's multi-threaded CPU matmul.
+    Used as the timed CPU baseline; returns bf16 bits."""
+    import torch
+
+    if threads:
+        lib().oracle_set_threads(threads)
+        torch.set_num_threads(threads)
+    w = torch.from_numpy(dequantize_f32(packed, scales, biases, bits, group))
+    x = torch.from_numpy(bf16_to_f32(np.asarray(x_bf16, dtype=np.uint16)))
+    y = x @ w.T
+    if bias is not None:
+        y = y + torch.from_numpy(bf16_to_f32(np.asarray(bias, dtype=np.uint16)))
+    return f32_to_bf16(y.numpy())

@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(256) qmm_dequantize_kernel(const uint32_t *__r
         float v[C];
 #pragma unroll
         for (int j = 0; j < C; ++j) {
-            const int64_t g = row * groups + (col0 + j) / group;
+            const int64_t g = row * groups + (int32_t)(col0 + j) / group;
             const float s = bf16_bits_to_f32(__ldg(scales + g));
             const float o = bf16_bits_to_f32(__ldg(offsets + g));
             v[j] = fmaf(q[j], s, o);
@@ -128,38 +128,123 @@ struct GemvParams {
     int32_t k;
     int32_t m;
     int32_t group;
+    int32_t cpg_shift;  // log2(group / codes per 16-byte chunk)
 };
 
-// Shared memory: xs[k][MT] (token-minor f32), then xsum[nchunks][MT].
+// Sum over one 16-byte chunk of codes of x_k * f(q_k) for every token, where
+// f is the float the code unpacks to.  4-bit codes unpack to 2 + q/64 (one
+// byte permute: exponent byte 0x40, code in the mantissa's top byte, exact),
+// so sum_k x_k q_k = 64 * S - 128 * X with X = sum_k x_k; 2- and 8-bit codes
+// unpack to q exactly (the 2^23 + q trick), so the sum is S itself.
+template <int BITS>
+struct ChunkAffine {
+    static constexpr float kMul = BITS == 4 ? 64.0f : 1.0f;   // sum x q = kMul * S + kAdd * X
+    static constexpr float kAdd = BITS == 4 ? -128.0f : 0.0f;
+};
+
+// Shared memory: xs[k][MP] (token-minor f32, MP = MT rounded up to a multiple
+// of 4 for vector loads; MP = 1 when MT = 1), then xsum[nchunks][MT].
+template <int MT>
+struct GemvPad {
+    static constexpr int kMP = MT == 1 ? 1 : (MT + 3) / 4 * 4;
+};
+
+template <int I>
+__device__ __forceinline__ float two_plus_q_over_64(uint32_t v) {
+    // bytes: [0x00, 0x00, v.b[I], 0x40]  ->  2 * (1 + q * 2^-7)
+    return __uint_as_float(__byte_perm(v, 0x40000000u, 0x7044u | (I << 8)));
+}
+
+template <int BITS, int MT>
+__device__ __forceinline__ void chunk_dot(const uint4 &w, const float *__restrict__ xc, float (&dot)[MT]) {
+    constexpr int CPW = 32 / BITS;
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        float q[CPW];
+        if constexpr (BITS == 4) {
+            const uint32_t lo = words[wi] & 0x0F0F0F0Fu, hi = (words[wi] >> 4) & 0x0F0F0F0Fu;
+            q[0] = two_plus_q_over_64<0>(lo);
+            q[1] = two_plus_q_over_64<0>(hi);
+            q[2] = two_plus_q_over_64<1>(lo);
+            q[3] = two_plus_q_over_64<1>(hi);
+            q[4] = two_plus_q_over_64<2>(lo);
+            q[5] = two_plus_q_over_64<2>(hi);
+            q[6] = two_plus_q_over_64<3>(lo);
+            q[7] = two_plus_q_over_64<3>(hi);
+        } else {
+            WordCodes<BITS>::unpack(words[wi], q);
+        }
+        if constexpr (MT == 1) {
+#pragma unroll
+            for (int j = 0; j < CPW; j += 4) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xc + wi * CPW + j);
+                dot[0] = fmaf(xv.x, q[j], dot[0]);
+                dot[0] = fmaf(xv.y, q[j + 1], dot[0]);
+                dot[0] = fmaf(xv.z, q[j + 2], dot[0]);
+                dot[0] = fmaf(xv.w, q[j + 3], dot[0]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < CPW; ++j) {
+                const float *xk = xc + (wi * CPW + j) * GemvPad<MT>::kMP;
+#pragma unroll
+                for (int t = 0; t < MT; t += 4) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(xk + t);
+                    dot[t] = fmaf(xv.x, q[j], dot[t]);
+                    if (t + 1 < MT) dot[t + 1] = fmaf(xv.y, q[j], dot[t + 1]);
+                    if (t + 2 < MT) dot[t + 2] = fmaf(xv.z, q[j], dot[t + 2]);
+                    if (t + 3 < MT) dot[t + 3] = fmaf(xv.w, q[j], dot[t + 3]);
+                }
+            }
+        }
+    }
+}
+
 template <int BITS, int MT>
 __global__ void __launch_bounds__(kGemvThreads) qmm_gemv_kernel(GemvParams p) {
     constexpr int CPC = 128 / BITS;  // codes per 16-byte chunk
-    constexpr int WPC = 4;           // words per chunk
-    constexpr int CPW = 32 / BITS;   // codes per word
-    extern __shared__ float gemv_smem[];
+    constexpr int MP = GemvPad<MT>::kMP;
+    extern __shared__ __align__(16) float gemv_smem[];
     const int k = p.k;
     const int nchunks = k / CPC;
     float *xs = gemv_smem;
-    float *xsum = gemv_smem + (size_t)k * MT;
+    float *xsum = gemv_smem + (size_t)k * MP;
 
-    // Stage x (tokens >= m read as zero) and per-chunk sums of x.
-    for (int i = threadIdx.x; i < k * MT; i += kGemvThreads) {
-        const int kk = i / MT, t = i - kk * MT;
-        xs[i] = t < p.m ? bf16_bits_to_f32(__ldg(p.x + (size_t)t * k + kk)) : 0.0f;
+    // Stage x as f32 (tokens >= m read as zero), 8 bf16 per load.
+    for (int i = threadIdx.x; i < (k / 8) * MP; i += kGemvThreads) {
+        const int t = i % MP, k8 = (i / MP) * 8;
+        float v[8];
+        if (t < p.m) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)t * k + k8));
+            const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[2 * j] = __uint_as_float(r[j] << 16);
+                v[2 * j + 1] = __uint_as_float(r[j] & 0xFFFF0000u);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xs[(size_t)(k8 + j) * MP + t] = v[j];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < nchunks * MT; i += kGemvThreads) {
         const int c = i / MT, t = i - c * MT;
         float sum = 0.0f;
-        for (int j = 0; j < CPC; ++j) sum += xs[(size_t)(c * CPC + j) * MT + t];
+        for (int j = 0; j < CPC; ++j) sum += xs[(size_t)(c * CPC + j) * MP + t];
         xsum[i] = sum;
     }
     __syncthreads();
 
     constexpr int kGemvRows = GemvShape<MT>::kRows;
     constexpr int kGemvUnroll = GemvShape<MT>::kUnroll;
+    constexpr float kMul = ChunkAffine<BITS>::kMul, kAdd = ChunkAffine<BITS>::kAdd;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t groups = k / p.group;
+    const int groups = k / p.group;
+    const int cpg_shift = p.cpg_shift;  // log2(chunks per group)
     const int64_t ntasks = (p.n + kGemvRows - 1) / kGemvRows;
     const uint4 *packed4 = reinterpret_cast<const uint4 *>(p.packed);
 
@@ -183,7 +268,7 @@ __global__ void __launch_bounds__(kGemvThreads) qmm_gemv_kernel(GemvParams p) {
                     const int64_t row = row0 + r;
                     const bool ok = c < nchunks && row < p.n;
                     wv[r][u] = ok ? ld_stream_u4(packed4 + row * nchunks + c) : make_uint4(0, 0, 0, 0);
-                    const int64_t g = row * groups + (int64_t)c * CPC / p.group;
+                    const int64_t g = row * groups + (c >> cpg_shift);
                     sc[r][u] = ok ? bf16_bits_to_f32(__ldg(p.scales + g)) : 0.0f;
                     of[r][u] = ok ? bf16_bits_to_f32(__ldg(p.offsets + g)) : 0.0f;
                 }
@@ -192,28 +277,18 @@ __global__ void __launch_bounds__(kGemvThreads) qmm_gemv_kernel(GemvParams p) {
             for (int u = 0; u < kGemvUnroll; ++u) {
                 const int c = cb + u * 32 + lane;
                 if (c >= nchunks) break;
-                const float *xc = xs + (size_t)c * CPC * MT;
+                const float *xc = xs + (size_t)c * CPC * MP;
 #pragma unroll
                 for (int r = 0; r < kGemvRows; ++r) {
                     float dot[MT];
 #pragma unroll
                     for (int t = 0; t < MT; ++t) dot[t] = 0.0f;
-                    const uint32_t words[WPC] = {wv[r][u].x, wv[r][u].y, wv[r][u].z, wv[r][u].w};
-#pragma unroll
-                    for (int wi = 0; wi < WPC; ++wi) {
-                        float q[CPW];
-                        WordCodes<BITS>::unpack(words[wi], q);
-#pragma unroll
-                        for (int j = 0; j < CPW; ++j) {
-                            const float *xk = xc + (size_t)(wi * CPW + j) * MT;
-#pragma unroll
-                            for (int t = 0; t < MT; ++t) dot[t] = fmaf(xk[t], q[j], dot[t]);
-                        }
-                    }
+                    chunk_dot<BITS, MT>(wv[r][u], xc, dot);
+                    const float a = sc[r][u] * kMul;
+                    const float b = fmaf(sc[r][u], kAdd, of[r][u]);
 #pragma unroll
                     for (int t = 0; t < MT; ++t)
-                        acc[r][t] = fmaf(sc[r][u], dot[t],
-                                         fmaf(of[r][u], xsum[(size_t)c * MT + t], acc[r][t]));
+                        acc[r][t] = fmaf(a, dot[t], fmaf(b, xsum[(size_t)c * MT + t], acc[r][t]));
                 }
             }
         }
@@ -256,7 +331,14 @@ static int gemv_tile(int64_t m) {
 
 static size_t gemv_smem_bytes(const qmm_weight &w, int mt) {
     const int cpc = 128 / w.bits;
-    return ((size_t)w.k * mt + (size_t)(w.k / cpc) * mt) * sizeof(float);
+    const int mp = mt == 1 ? 1 : (mt + 3) / 4 * 4;
+    return ((size_t)w.k * mp + (size_t)(w.k / cpc) * mt) * sizeof(float);
+}
+
+static int log2_exact(int v) {
+    int s = 0;
+    while ((1 << s) < v) ++s;
+    return (1 << s) == v ? s : -1;
 }
 
 bool gemv_supported(const qmm_weight &w, int64_t m) {
@@ -264,6 +346,7 @@ bool gemv_supported(const qmm_weight &w, int64_t m) {
     if (w.bits != 2 && w.bits != 4 && w.bits != 8) return false;
     const int cpc = 128 / w.bits;
     if (w.k % cpc != 0 || w.group % cpc != 0) return false;
+    if (log2_exact(w.group / cpc) < 0) return false;
     if (w.k > (1 << 30)) return false;
     return gemv_smem_bytes(w, gemv_tile(m)) <= kGemvMaxSmem;
 }
@@ -307,6 +390,7 @@ qmm_status launch_gemv(const qmm_weight &w, const uint16_t *x, int64_t m, const 
     p.k = (int32_t)w.k;
     p.m = (int32_t)m;
     p.group = w.group;
+    p.cpg_shift = log2_exact(w.group / (128 / w.bits));
     const int mt = gemv_tile(m);
     const size_t smem = gemv_smem_bytes(w, mt);
 #define QMM_GEMV_CASE(B, MT) \
