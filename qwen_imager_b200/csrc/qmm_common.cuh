@@ -71,14 +71,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One try_wait: the thread sleeps until the phase completes or about
+// kSuspendHintNs elapse, so a waiting warp does not spin on the issue slots.
+constexpr uint32_t kSuspendHintNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -91,14 +95,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t spin = 1;; ++spin) {
+    for (;;) {
         if (mbar_try_wait(addr, parity)) return true;
-        if ((spin & 63u) == 0) {
-            if (*reinterpret_cast<volatile uint32_t *>(err) != kErrNone) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-                atomicCAS(err, kErrNone, code);
-                return false;
-            }
+        if (*reinterpret_cast<volatile uint32_t *>(err) != kErrNone) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(err, kErrNone, code);
+            return false;
         }
     }
 }
@@ -247,6 +249,31 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
     return __uint_as_float(bits16 << 16);
+}
+
+// Packed f32x2 arithmetic of sm_100 (two independent IEEE round-to-nearest
+// operations per instruction).
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+    uint64_t d;
+    asm("{\n\t.reg .b64 ra, rb;\n\t"
+        "mov.b64 ra, {%1, %2};\n\t"
+        "mov.b64 rb, {%3, %4};\n\t"
+        "add.rn.f32x2 %0, ra, rb;\n\t}\n"
+        : "=l"(d)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+        "mov.b64 ra, {%1, %2};\n\t"
+        "mov.b64 rb, {%3, %4};\n\t"
+        "mov.b64 rc, {%5, %6};\n\t"
+        "fma.rn.f32x2 %0, ra, rb, rc;\n\t}\n"
+        : "=l"(d)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
 }
 
 }  // namespace qmm

@@ -85,7 +85,7 @@ struct Params {
     uint16_t *y;
     EpilogueArgs ep;
     int32_t m, n, k;
-    int32_t group, groups;
+    int32_t group, groups, group_shift;
     int32_t w_tiles, num_tiles;
     uint32_t *err;
 };
@@ -108,15 +108,16 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // 32-code halves (a group of 32 each when group == 32)
         const uint32_t mh = h == 0 ? m0 : m1;
-        const float sc = bf16_bits_to_f32(mh & 0xFFFFu);
-        const float of = bf16_bits_to_f32(mh >> 16);
+        const float sc1 = bf16_bits_to_f32(mh & 0xFFFFu);
+        const float of1 = bf16_bits_to_f32(mh >> 16);
+        const float2 sc = make_float2(sc1, sc1), of = make_float2(of1, of1);
         if constexpr (BITS == 4) {
             const uint4 w4 = *reinterpret_cast<const uint4 *>(pst + packed_chunk_offset<4>(row, h));
             const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 uint32_t o4[4];
-                dequant_word_bf16x2<4>(ws[j], sc, of, o4);
+                dequant_word_bf16x2_packed<4>(ws[j], sc, of, o4);
 #pragma unroll
                 for (int t = 0; t < 4; ++t) a[h * 16 + j * 4 + t] = o4[t];
             }
@@ -128,7 +129,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t o2[2];
-                    dequant_word_bf16x2<8>(ws[j], sc, of, o2);
+                    dequant_word_bf16x2_packed<8>(ws[j], sc, of, o2);
                     a[h * 16 + cc * 8 + j * 2 + 0] = o2[0];
                     a[h * 16 + cc * 8 + j * 2 + 1] = o2[1];
                 }
@@ -269,27 +270,30 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
         const int set = (warp - W::kDq0) >> 2;     // blocks i with i % SETS == set
         const int row = quad * 32 + lane;          // weight row within the tile
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-        // Scale/offset of this thread's row for block (tile_local, kb), one block ahead.
+        // Scale/offset of this thread's row for block (tile_local, kb), one
+        // block ahead.  Group index of codes [0,32) / [32,64) of block kb:
+        // (kb * 64) >> log2(group) and (kb * 64 + 32) >> log2(group).
+        const int gshift = p.group_shift;
         auto load_meta = [&](int tile_local, int kb, uint32_t &m0, uint32_t &m1) {
             m0 = m1 = 0;
             const int tile = (int)blockIdx.x + tile_local * (int)gridDim.x;
-            const int64_t n = (int64_t)(tile % p.w_tiles) * kWRows + row;
+            const int wt = tile - (tile / p.w_tiles) * p.w_tiles;
+            const int n = wt * kWRows + row;
             if (tile < p.num_tiles && n < p.n) {
-                const int64_t base = n * p.groups;
-                const int g0 = (kb * kBK) / p.group;
-                const int g1 = (kb * kBK + 32) / p.group;
-                m0 = (uint32_t)__ldg(p.scales + base + g0) | ((uint32_t)__ldg(p.offsets + base + g0) << 16);
-                m1 = g1 == g0 ? m0
-                              : ((uint32_t)__ldg(p.scales + base + g1) |
-                                 ((uint32_t)__ldg(p.offsets + base + g1) << 16));
+                const uint16_t *sp = p.scales + (int64_t)n * p.groups;
+                const uint16_t *op = p.offsets + (int64_t)n * p.groups;
+                const int g0 = (kb * kBK) >> gshift;
+                const int g1 = (kb * kBK + 32) >> gshift;
+                m0 = (uint32_t)__ldg(sp + g0) | ((uint32_t)__ldg(op + g0) << 16);
+                m1 = g1 == g0 ? m0 : ((uint32_t)__ldg(sp + g1) | ((uint32_t)__ldg(op + g1) << 16));
             }
         };
-        int tl = set / nkb, kb = set % nkb;
+        int tl = set / nkb, kb = set - (set / nkb) * nkb;
         uint32_t m0 = 0, m1 = 0;
         if ((uint32_t)set < total_blocks) load_meta(tl, kb, m0, m1);
+        int s = set % S, a = set % kASlots;
+        uint32_t ph_s = (set / S) & 1, ph_a = (set / kASlots) & 1;
         for (uint32_t i = set; i < total_blocks; i += SETS) {
-            const int s = i % S;
-            const int a = i % kASlots;
             int ntl = tl, nkb_i = kb + SETS;
             while (nkb_i >= nkb) {
                 nkb_i -= nkb;
@@ -297,8 +301,8 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
             }
             uint32_t n0m = 0, n1m = 0;
             if (i + SETS < total_blocks) load_meta(ntl, nkb_i, n0m, n1m);
-            if (!mbar_wait(&full[s], (i / S) & 1, p.err, kErrTimeoutDequant) ||
-                !mbar_wait(&aempty[a], ((i / kASlots) & 1) ^ 1, p.err, kErrTimeoutDequant))
+            if (!mbar_wait(&full[s], ph_s, p.err, kErrTimeoutDequant) ||
+                !mbar_wait(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant))
                 break;
             uint32_t v[32];
             dequant_row_block<BITS>(smem + C::kPOff + s * C::kPStageBytes, m0, m1, row, v);
@@ -313,6 +317,16 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
             m1 = n1m;
             tl = ntl;
             kb = nkb_i;
+            s += SETS;
+            if (s >= S) {
+                s -= S;
+                ph_s ^= 1;
+            }
+            a += SETS;
+            if (a >= kASlots) {
+                a -= kASlots;
+                ph_a ^= 1;
+            }
         }
     } else {
         // ---------------------------------------------------------- epilogue
@@ -441,6 +455,8 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.k = (int32_t)w.k;
     p.group = w.group;
     p.groups = (int32_t)(w.k / w.group);
+    p.group_shift = 0;
+    while ((1 << p.group_shift) < w.group) ++p.group_shift;
     p.w_tiles = (int32_t)((w.n + kWRows - 1) / kWRows);
     const int64_t t_tiles = (m + T - 1) / T;
     p.num_tiles = (int32_t)(p.w_tiles * t_tiles);
@@ -458,6 +474,7 @@ bool gemm_supported(const qmm_weight &w) {
     if (w.bits != 4 && w.bits != 8) return false;
     if (w.k % gemm::kBK != 0) return false;
     if (!(w.group == 32 || w.group % gemm::kBK == 0)) return false;
+    if ((w.group & (w.group - 1)) != 0) return false;  // power-of-two groups (MLX: 32, 64, 128)
     if (w.n > (int64_t)INT32_MAX - gemm::kWRows || w.k > (int64_t)INT32_MAX / 8) return false;
     return true;
 }

@@ -94,4 +94,44 @@ __device__ __forceinline__ void dequant_word_bf16x2(uint32_t w, float s, float o
         out[i] = pack_bf16x2_rn(fmaf(q[2 * i], s, o), fmaf(q[2 * i + 1], s, o));
 }
 
+// Same result as dequant_word_bf16x2 with the subtraction of 2^23 and the
+// multiply-add done as packed f32x2 operations (half the FMA-pipe instructions).
+template <int I>
+__device__ __forceinline__ uint32_t magic_byte_bits(uint32_t v) {
+    return __byte_perm(v, 0x4B000000u, 0x7440u + I);
+}
+
+template <int BITS>
+__device__ __forceinline__ void dequant_word_bf16x2_packed(uint32_t w, float2 s2, float2 o2,
+                                                           uint32_t (&out)[WordCodes<BITS>::kCount / 2]) {
+    constexpr int C = WordCodes<BITS>::kCount;
+    const float2 neg_magic = make_float2(-kMagic23, -kMagic23);
+    uint32_t m[C];
+    if constexpr (BITS == 8) {
+        m[0] = magic_byte_bits<0>(w);
+        m[1] = magic_byte_bits<1>(w);
+        m[2] = magic_byte_bits<2>(w);
+        m[3] = magic_byte_bits<3>(w);
+    } else if constexpr (BITS == 4) {
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        m[0] = magic_byte_bits<0>(lo);
+        m[1] = magic_byte_bits<0>(hi);
+        m[2] = magic_byte_bits<1>(lo);
+        m[3] = magic_byte_bits<1>(hi);
+        m[4] = magic_byte_bits<2>(lo);
+        m[5] = magic_byte_bits<2>(hi);
+        m[6] = magic_byte_bits<3>(lo);
+        m[7] = magic_byte_bits<3>(hi);
+    } else {
+        static_assert(BITS == 4 || BITS == 8, "packed path covers 4- and 8-bit codes");
+    }
+#pragma unroll
+    for (int i = 0; i < C / 2; ++i) {
+        const float2 f = make_float2(__uint_as_float(m[2 * i]), __uint_as_float(m[2 * i + 1]));
+        const float2 q = add_f32x2(f, neg_magic);
+        const float2 v = fma_f32x2(q, s2, o2);
+        out[i] = pack_bf16x2_rn(v.x, v.y);
+    }
+}
+
 }  // namespace qmm
