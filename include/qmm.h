@@ -97,7 +97,8 @@ typedef struct qmm_epilogue {
 typedef enum qmm_path {
     QMM_PATH_AUTO = 0,   /* m <= 16: GEMV, otherwise the tcgen05 GEMM */
     QMM_PATH_GEMV = 1,   /* warp-per-row streaming kernel, any m (slow for large m) */
-    QMM_PATH_GEMM = 2    /* tcgen05/TMEM GEMM, any m >= 1 */
+    QMM_PATH_GEMM = 2,   /* tcgen05/TMEM GEMM, any m >= 1 */
+    QMM_PATH_GEMM_PAIR = 3  /* the GEMM on CTA pairs (cta_group::2, MMA M = 256) */
 } qmm_path;
 
 /* ABI version of the loaded library (QMM_ABI_VERSION at build time). */

@@ -42,6 +42,7 @@ QMM_ACT_SILU = 2
 QMM_PATH_AUTO = 0
 QMM_PATH_GEMV = 1
 QMM_PATH_GEMM = 2
+QMM_PATH_GEMM_PAIR = 3
 
 # Every symbol include/qmm.h declares.
 EXPORTED_SYMBOLS = (

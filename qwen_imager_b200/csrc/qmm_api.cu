@@ -154,7 +154,7 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
     if (m < 0) return fail(QMM_ERR_BAD_SHAPE, "negative token count %lld", (long long)m);
     if (m == 0) return QMM_OK;
     if (!x || !y) return fail(QMM_ERR_INVALID_ARGUMENT, "null x or y");
-    if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM)
+    if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM_PAIR)
         return fail(QMM_ERR_INVALID_ARGUMENT, "unknown path %d", path);
     qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
     if (e.activation < QMM_ACT_NONE || e.activation > QMM_ACT_SILU)
@@ -168,8 +168,11 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
     }
     if ((s = check_device()) != QMM_OK) return s;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (path == QMM_PATH_AUTO) path = (m <= 16 && qmm::gemv_supported(*w, m)) ? QMM_PATH_GEMV : QMM_PATH_GEMM;
+    if (path == QMM_PATH_AUTO)
+        path = (m <= 16 && (qmm::gemv_tma_supported(*w, m) || qmm::gemv_supported(*w, m))) ? QMM_PATH_GEMV
+                                                                                           : QMM_PATH_GEMM;
     if (path == QMM_PATH_GEMV) {
+        if (qmm::gemv_tma_supported(*w, m)) return qmm::launch_gemv_tma(*w, x, m, e, y, st);
         if (!qmm::gemv_supported(*w, m))
             return fail(QMM_ERR_UNSUPPORTED,
                         "gemv: %d-bit, group %d, k=%lld, m=%lld is outside the kernel's layouts",
@@ -181,7 +184,7 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
                     "gemm: %d-bit, group %d, k=%lld is outside the kernel's layouts (needs 4/8-bit, "
                     "k %% 64 == 0, group 32 or a multiple of 64)",
                     w->bits, w->group, (long long)w->k);
-    return qmm::launch_gemm(*w, x, m, e, y, st);
+    return qmm::launch_gemm(*w, x, m, e, y, path == QMM_PATH_GEMM_PAIR, st);
 }
 
 qmm_status qmm_linear(const qmm_weight *w, const uint16_t *x, int64_t m, const qmm_epilogue *ep,

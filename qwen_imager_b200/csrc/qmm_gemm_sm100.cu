@@ -27,7 +27,6 @@
 // Every wait is bounded (qmm_common.cuh): on expiry the CTA records an error
 // code, drains its own in-flight copies and MMAs, frees TMEM and exits.
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 #include "qmm_epilogue.cuh"
@@ -39,35 +38,42 @@ namespace gemm {
 
 constexpr int kWRows = 128;  // weight rows per tile = TMEM lanes = MMA M
 constexpr int kBK = 64;      // K per pipeline block (4 MMAs of K = 16)
-constexpr int kASlots = 4;   // TMEM A slots (32 columns each)
 constexpr int kEpiWarps = 4;
 constexpr int kTmemCols = 512;
 
-// Warp layout: epilogue warps 0-3, dequant warps 4 .. 4 + 4*SETS - 1 (set j
-// handles K-blocks i with i % SETS == j, quadrant = warp % 4), then the
-// producer warp and the MMA warp.
-template <int SETS>
+// Warp layout: epilogue warps 0-3, then 4 * SETS * HALVES dequant warps (set
+// j handles K-blocks i with i % SETS == j; within a set, warp quadrant q and
+// half h dequantize codes [32 h, 32 h + 32) of rows 32 q .. 32 q + 31), then
+// the producer warp and the MMA warp.
+template <int SETS, int HALVES>
 struct Warps {
     static constexpr int kDq0 = kEpiWarps;
-    static constexpr int kDqWarps = 4 * SETS;
+    static constexpr int kPerSet = 4 * HALVES;
+    static constexpr int kDqWarps = kPerSet * SETS;
     static constexpr int kProducer = kDq0 + kDqWarps;
     static constexpr int kMma = kProducer + 1;
     static constexpr int kThreads = (kMma + 1) * 32;
 };
 
-template <int BITS, int T>
+// T: tokens per tile (MMA N, accumulator columns).  PAIR: the tile spans a CTA
+// pair (cta_group::2, MMA M = 256), each CTA holding 128 weight rows and T/2
+// of the tile's tokens in shared memory.
+template <int BITS, int T, bool PAIR>
 struct Cfg {
     static_assert(T % 32 == 0 && T >= 32 && T <= 256, "token tile");
-    static constexpr int kXStageBytes = T * kBK * 2;               // bf16 [T][64], 128B-swizzled
+    static constexpr int kXRows = PAIR ? T / 2 : T;                // x rows staged per CTA
+    static constexpr int kXStageBytes = kXRows * kBK * 2;          // bf16 [kXRows][64], 128B-swizzled
     static constexpr int kPWords = kBK * BITS / 32;                // packed words per row per block
     static constexpr int kPStageBytes = kWRows * kPWords * 4;      // uint32 [128][kPWords], swizzled
     static constexpr int kStageBytes = kXStageBytes + kPStageBytes;
+    // TMEM: two T-column accumulators, the rest as 32-column A slots (at most 8).
+    static constexpr int kASlots = (512 - 2 * T) / 32 > 8 ? 8 : (512 - 2 * T) / 32;
     static constexpr int kSmemBudget = 227 * 1024 - 2048;
     static constexpr int kStages = kSmemBudget / kStageBytes > 8 ? 8 : kSmemBudget / kStageBytes;
     static constexpr int kXOff = 0;
     static constexpr int kPOff = kXOff + kStages * kXStageBytes;
     static constexpr int kBarOff = kPOff + kStages * kPStageBytes;
-    static constexpr int kNumBars = 2 * kStages + 2 * kASlots + 4 + 1;
+    static constexpr int kNumBars = 3 * kStages + 2 * 8 + 4 + 1;
     static constexpr int kTmemPtrOff = kBarOff + kNumBars * 8;
     static constexpr int kSmemBytes = kTmemPtrOff + 16 + 1024;  // + alignment slack
     static constexpr int kAcc0 = 0;                              // accumulator b at b*T
@@ -76,7 +82,7 @@ struct Cfg {
     static_assert(2 * T + kASlots * 32 <= kTmemCols, "TMEM budget");
     static_assert(kXStageBytes % 1024 == 0 && kPStageBytes % 1024 == 0, "stage alignment");
     static_assert(kSmemBytes <= 232448, "shared memory");
-    static constexpr uint32_t kIdesc = idesc_bf16_f32(kWRows, T);
+    static constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * kWRows : kWRows, T);
 };
 
 struct Params {
@@ -101,13 +107,15 @@ __device__ __forceinline__ uint32_t packed_chunk_offset(int r, int c) {
 // Dequantizes the 64 codes of weight row `row` of one pipeline block into 32
 // bf16 pairs (k order), bit-exact with the reference's f32-then-bf16 rounding.
 // m0 / m1 = scale | offset << 16 (bf16 bits) of the groups holding codes
-// [0, 32) and [32, 64) of the block (equal unless group == 32).
-template <int BITS>
+// [0, 32) and [32, 64) of the block (equal unless group == 32).  NH halves
+// starting at half H0 (or at `hbase` when H0 < 0) are produced.
+template <int BITS, int H0, int NH>
 __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m0, uint32_t m1, int row,
-                                                  uint32_t (&a)[32]) {
+                                                  uint32_t (&a)[16 * NH], int hbase) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {  // 32-code halves (a group of 32 each when group == 32)
-        const uint32_t mh = h == 0 ? m0 : m1;
+    for (int hh = 0; hh < NH; ++hh) {  // 32-code halves (a group of 32 each when group == 32)
+        const int h = H0 >= 0 ? H0 + hh : hbase + hh;
+        const uint32_t mh = hh == 0 ? m0 : m1;
         const float sc1 = bf16_bits_to_f32(mh & 0xFFFFu);
         const float of1 = bf16_bits_to_f32(mh >> 16);
         const float2 sc = make_float2(sc1, sc1), of = make_float2(of1, of1);
@@ -119,7 +127,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
                 uint32_t o4[4];
                 dequant_word_bf16x2_packed<4>(ws[j], sc, of, o4);
 #pragma unroll
-                for (int t = 0; t < 4; ++t) a[h * 16 + j * 4 + t] = o4[t];
+                for (int t = 0; t < 4; ++t) a[hh * 16 + j * 4 + t] = o4[t];
             }
         } else {
 #pragma unroll
@@ -130,26 +138,29 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
                 for (int j = 0; j < 4; ++j) {
                     uint32_t o2[2];
                     dequant_word_bf16x2_packed<8>(ws[j], sc, of, o2);
-                    a[h * 16 + cc * 8 + j * 2 + 0] = o2[0];
-                    a[h * 16 + cc * 8 + j * 2 + 1] = o2[1];
+                    a[hh * 16 + cc * 8 + j * 2 + 0] = o2[0];
+                    a[hh * 16 + cc * 8 + j * 2 + 1] = o2[1];
                 }
             }
         }
     }
 }
 
-template <int BITS, int T, int SETS>
-__global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
+template <int BITS, int T, int SETS, int HALVES, bool PAIR>
+__global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w, const Params p) {
-    using C = Cfg<BITS, T>;
-    using W = Warps<SETS>;
+    using C = Cfg<BITS, T, PAIR>;
+    using W = Warps<SETS, HALVES>;
     constexpr int S = C::kStages;
+    constexpr int kASlots = C::kASlots;
+    constexpr int kTileRows = PAIR ? 2 * kWRows : kWRows;  // weight rows per (pair) tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);  // [S] x + codes + meta landed
-    uint64_t *sempty = full + S;                                       // [S] stage consumed
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::kBarOff);  // [S] this CTA's stage landed
+    uint64_t *xfull = full + S;                                        // [S] PAIR: both x halves (leader)
+    uint64_t *sempty = xfull + S;                                      // [S] stage consumed
     uint64_t *afull = sempty + S;                                      // [A] A slot written
     uint64_t *aempty = afull + kASlots;                                // [A] MMAs reading the slot done
     uint64_t *acc_full = aempty + kASlots;                             // [2] tile accumulated
@@ -159,26 +170,38 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    constexpr int kPairCtas = PAIR ? 2 : 1;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = the pair's leader (issues MMAs)
+    const bool leader = rank == 0;
+    // Scheduling unit: one CTA, or one CTA pair (cluster of two).
+    const int unit = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+    const int nunits = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&sempty[s], 1 + 4);  // MMA commit + the 4 dequant warps of the block's set
+            mbar_init(&xfull[s], 1);
+            mbar_init(&sempty[s], 1 + W::kPerSet);  // MMA commit + the dequant warps of the block's set
         }
         for (int a = 0; a < kASlots; ++a) {
-            mbar_init(&afull[a], 4);
+            mbar_init(&afull[a], kPairCtas * W::kPerSet);
             mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kEpiWarps);
+            mbar_init(&acc_empty[b], kPairCtas * kEpiWarps);
         }
         mbar_init(drain, 1);
         fence_barrier_init();
     }
     if (warp == W::kMma) {
-        tmem_alloc(tmem_slot, kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, kTmemCols);
+            tmem_relinquish();
+        }
     }
     if (warp == W::kProducer && lane == 0) {
         tma_prefetch_desc(&tmap_x);
@@ -186,136 +209,195 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
     }
     tc_fence_before_sync();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // peer barriers initialized, TMEM allocated in both CTAs
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     const int nkb = p.k / kBK;
-    const int local_tiles = (p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int local_tiles = (p.num_tiles - unit + nunits - 1) / nunits;
     const uint32_t total_blocks = (uint32_t)local_tiles * (uint32_t)nkb;
+    // Barriers of the pair's leader that every CTA of the pair signals.
+    auto leader_bar = [&](uint64_t *bar) { return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
+    auto arrive_leader = [&](uint64_t *bar) {
+        if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
+        else mbar_arrive(bar);
+    };
 
     if (warp == W::kProducer) {
         // ---------------------------------------------------------- producer
         uint32_t i = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-            const int n0 = (tile % p.w_tiles) * kWRows;
-            const int m0 = (tile / p.w_tiles) * T;
+        int s = 0;
+        uint32_t ph_s = 0;
+        for (int tile = unit; ok && tile < p.num_tiles; tile += nunits) {
+            const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
+            const int m0 = (tile / p.w_tiles) * T + (int)rank * C::kXRows;
             for (int kb = 0; kb < nkb; ++kb, ++i) {
-                const int s = i % S;
-                if (!mbar_wait(&sempty[s], ((i / S) & 1) ^ 1, p.err, kErrTimeoutProducer)) {
+                if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], C::kXStageBytes + C::kPStageBytes);
-                    tma_load_2d(smem + C::kXOff + s * C::kXStageBytes, &tmap_x, &full[s], kb * kBK, m0);
+                    if constexpr (PAIR) {
+                        // Both x halves complete on the leader's xfull; codes on this CTA's full.
+                        if (leader) mbar_arrive_expect_tx(&xfull[s], 2 * C::kXStageBytes);
+                        tma_load_2d_pair(smem + C::kXOff + s * C::kXStageBytes, &tmap_x, leader_bar(&xfull[s]),
+                                         kb * kBK, m0);
+                        mbar_arrive_expect_tx(&full[s], C::kPStageBytes);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], C::kXStageBytes + C::kPStageBytes);
+                        tma_load_2d(smem + C::kXOff + s * C::kXStageBytes, &tmap_x, &full[s], kb * kBK, m0);
+                    }
                     tma_load_2d(smem + C::kPOff + s * C::kPStageBytes, &tmap_w, &full[s], kb * C::kPWords, n0);
                 }
                 __syncwarp();
+                if (++s == S) {
+                    s = 0;
+                    ph_s ^= 1;
+                }
             }
         }
         if (!ok) {
             // Let the copies already issued land before the CTA exits.
             const uint32_t first = i > (uint32_t)S ? i - S : 0;
             for (uint32_t j = first; j < i; ++j)
-                mbar_wait(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain);
+                mbar_wait<PAIR>(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain);
         }
     } else if (warp == W::kMma) {
         // ---------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            uint32_t i = 0;
-            int lt = 0;
+        if (lane == 0 && leader) {
+            // Kept to a handful of instructions per block: this thread shares its
+            // SM sub-partition with dequantization warps, and every cycle it
+            // waits for an issue slot delays the tensor pipe.
             bool ok = true;
             bool issued = false;
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++lt) {
+            constexpr uint16_t kBoth = 0x3;
+            const uint64_t bdesc0 = sdesc_kmajor_sw128(smem_u32(smem + C::kXOff));
+            constexpr uint64_t kBStep = C::kXStageBytes >> 4;  // descriptor start-address units
+            int s = 0, a = 0;
+            uint32_t ph_s = 0, ph_a = 0;
+            int lt = 0;
+            for (int tile = unit; ok && tile < p.num_tiles; tile += nunits, ++lt) {
                 const int b = lt & 1;
-                const uint32_t u = lt >> 1;
-                if (!mbar_wait(&acc_empty[b], (u & 1) ^ 1, p.err, kErrTimeoutMma)) {
+                if (!mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after_sync();
                 const uint32_t d = tmem + C::kAcc0 + b * T;
-                for (int kb = 0; kb < nkb; ++kb, ++i) {
-                    const int s = i % S;
-                    const int a = i % kASlots;
-                    if (!mbar_wait(&afull[a], (i / kASlots) & 1, p.err, kErrTimeoutMma) ||
-                        !mbar_wait(&full[s], (i / S) & 1, p.err, kErrTimeoutMma)) {
+                uint32_t acc = 0;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma) ||
+                        !mbar_wait<PAIR>(PAIR ? &xfull[s] : &full[s], ph_s, p.err, kErrTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after_sync();
                     const uint32_t atm = tmem + C::kASlot0 + a * 32;
-                    const uint64_t bdesc =
-                        sdesc_kmajor_sw128(smem_u32(smem + C::kXOff + s * C::kXStageBytes));
+                    const uint64_t bdesc = bdesc0 + (uint64_t)s * kBStep;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk)
-                        tc_mma_ts(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc,
-                                  (kb | kk) != 0 ? 1u : 0u);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        if constexpr (PAIR) tc_mma_ts_pair(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
+                        else tc_mma_ts(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
+                        acc = 1;
+                    }
                     issued = true;
-                    tc_commit(&aempty[a]);
-                    tc_commit(&sempty[s]);
+                    if constexpr (PAIR) {
+                        tc_commit_pair_multicast(&aempty[a], kBoth);
+                        tc_commit_pair_multicast(&sempty[s], kBoth);
+                    } else {
+                        tc_commit(&aempty[a]);
+                        tc_commit(&sempty[s]);
+                    }
+                    if (++s == S) {
+                        s = 0;
+                        ph_s ^= 1;
+                    }
+                    if (++a == kASlots) {
+                        a = 0;
+                        ph_a ^= 1;
+                    }
                 }
                 if (!ok) break;
-                tc_commit(&acc_full[b]);
+                if constexpr (PAIR) tc_commit_pair_multicast(&acc_full[b], kBoth);
+                else tc_commit(&acc_full[b]);
             }
             if (!ok && issued) {
-                tc_commit(drain);
-                mbar_wait(drain, 0, p.err, kErrTimeoutDrain);
+                if constexpr (PAIR) tc_commit_pair_multicast(drain, 0x1);
+                else tc_commit(drain);
+                mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain);
             }
         }
         __syncwarp();
     } else if (warp >= W::kDq0) {
         // ---------------------------------------------------------- dequant
-        const int quad = warp & 3;                 // TMEM lane quadrant
-        const int set = (warp - W::kDq0) >> 2;     // blocks i with i % SETS == set
-        const int row = quad * 32 + lane;          // weight row within the tile
-        const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-        // Scale/offset of this thread's row for block (tile_local, kb), one
-        // block ahead.  Group index of codes [0,32) / [32,64) of block kb:
-        // (kb * 64) >> log2(group) and (kb * 64 + 32) >> log2(group).
+        const int quad = warp & 3;                          // TMEM lane quadrant
+        const int widx = warp - W::kDq0;
+        const int set = widx / W::kPerSet;                  // blocks i with i % SETS == set
+        const int half = (widx % W::kPerSet) >> 2;          // HALVES == 2: codes [32 half, 32 half + 32)
+        const int row = quad * 32 + lane;                   // weight row within the tile
+        const uint32_t tcol = tmem + (static_cast<uint32_t>(quad * 32) << 16) + C::kASlot0 + half * 16;
         const int gshift = p.group_shift;
-        auto load_meta = [&](int tile_local, int kb, uint32_t &m0, uint32_t &m1) {
-            m0 = m1 = 0;
-            const int tile = (int)blockIdx.x + tile_local * (int)gridDim.x;
-            const int wt = tile - (tile / p.w_tiles) * p.w_tiles;
-            const int n = wt * kWRows + row;
+        // This thread's scale/offset row pointers for a tile (null past n).
+        const uint16_t *sp = nullptr, *op = nullptr;
+        auto set_tile = [&](int tile_local) {
+            const int tile = unit + tile_local * nunits;
+            const int n = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows + row;
+            sp = op = nullptr;
             if (tile < p.num_tiles && n < p.n) {
-                const uint16_t *sp = p.scales + (int64_t)n * p.groups;
-                const uint16_t *op = p.offsets + (int64_t)n * p.groups;
-                const int g0 = (kb * kBK) >> gshift;
-                const int g1 = (kb * kBK + 32) >> gshift;
+                sp = p.scales + (int64_t)n * p.groups;
+                op = p.offsets + (int64_t)n * p.groups;
+            }
+        };
+        // (scale | offset << 16) of the group(s) this warp needs in block kb.
+        auto load_meta = [&](int kb, uint32_t &m0, uint32_t &m1) {
+            m0 = m1 = 0;
+            if (sp) {
+                const int c0 = kb * kBK + (HALVES == 2 ? half * 32 : 0);
+                const int g0 = c0 >> gshift;
+                const int g1 = (c0 + 32) >> gshift;
                 m0 = (uint32_t)__ldg(sp + g0) | ((uint32_t)__ldg(op + g0) << 16);
-                m1 = g1 == g0 ? m0 : ((uint32_t)__ldg(sp + g1) | ((uint32_t)__ldg(op + g1) << 16));
+                if (HALVES == 1) m1 = g1 == g0 ? m0 : ((uint32_t)__ldg(sp + g1) | ((uint32_t)__ldg(op + g1) << 16));
             }
         };
         int tl = set / nkb, kb = set - (set / nkb) * nkb;
+        set_tile(tl);
         uint32_t m0 = 0, m1 = 0;
-        if ((uint32_t)set < total_blocks) load_meta(tl, kb, m0, m1);
+        if ((uint32_t)set < total_blocks) load_meta(kb, m0, m1);
         int s = set % S, a = set % kASlots;
         uint32_t ph_s = (set / S) & 1, ph_a = (set / kASlots) & 1;
         for (uint32_t i = set; i < total_blocks; i += SETS) {
-            int ntl = tl, nkb_i = kb + SETS;
-            while (nkb_i >= nkb) {
-                nkb_i -= nkb;
-                ++ntl;
+            // Advance to the next block of this set and prefetch its scales.
+            int nkb_i = kb + SETS;
+            if (nkb_i >= nkb) {
+                while (nkb_i >= nkb) {
+                    nkb_i -= nkb;
+                    ++tl;
+                }
+                set_tile(tl);
             }
             uint32_t n0m = 0, n1m = 0;
-            if (i + SETS < total_blocks) load_meta(ntl, nkb_i, n0m, n1m);
-            if (!mbar_wait(&full[s], ph_s, p.err, kErrTimeoutDequant) ||
-                !mbar_wait(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant))
+            if (i + SETS < total_blocks) load_meta(nkb_i, n0m, n1m);
+            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant) ||
+                !mbar_wait<PAIR>(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant))
                 break;
-            uint32_t v[32];
-            dequant_row_block<BITS>(smem + C::kPOff + s * C::kPStageBytes, m0, m1, row, v);
-            tmem_st_32x32b_x32(tmem + lane_addr + C::kASlot0 + a * 32, v);
+            const uint8_t *pst = smem + C::kPOff + s * C::kPStageBytes;
+            if constexpr (HALVES == 1) {
+                uint32_t v[32];
+                dequant_row_block<BITS, 0, 2>(pst, m0, m1, row, v, 0);
+                tmem_st_32x32b_x32(tcol + a * 32, v);
+            } else {
+                uint32_t v[16];
+                dequant_row_block<BITS, -1, 1>(pst, m0, m0, row, v, half);
+                tmem_st_32x32b_x16(tcol + a * 32, v);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
             tc_wait_st();
             tc_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&afull[a]);
+            if (lane == 0) arrive_leader(&afull[a]);
             m0 = n0m;
             m1 = n1m;
-            tl = ntl;
             kb = nkb_i;
             s += SETS;
             if (s >= S) {
@@ -333,12 +415,12 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
         const int quad = warp;
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int lt = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+        for (int tile = unit; tile < p.num_tiles; tile += nunits, ++lt) {
             const int b = lt & 1;
             const uint32_t u = lt >> 1;
-            const int n0 = (tile % p.w_tiles) * kWRows;
+            const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
             const int m0 = (tile / p.w_tiles) * T;
-            if (!mbar_wait(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue)) break;
+            if (!mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue)) break;
             tc_fence_after_sync();
             const int64_t n = n0 + quad * 32 + lane;
             const bool nvalid = n < p.n;
@@ -352,7 +434,7 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
                     // Accumulator drained into registers: let the MMA reuse it.
                     tc_fence_before_sync();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+                    if (lane == 0) arrive_leader(&acc_empty[b]);
                 }
                 if (nvalid) {
 #pragma unroll
@@ -375,9 +457,11 @@ __global__ void __launch_bounds__(Warps<SETS>::kThreads, 1)
     __syncwarp();
     tc_fence_before_sync();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // the peer is done with this CTA's TMEM and barriers
     if (warp == W::kMma) {
         tc_fence_after_sync();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, kTmemCols);
+        else tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -419,24 +503,24 @@ static qmm_status make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, int e
     return QMM_OK;
 }
 
-template <int BITS, int T, int SETS>
+template <int BITS, int T, int SETS, int HALVES, bool PAIR>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
                            const qmm_epilogue &ep, uint16_t *y, cudaStream_t st) {
-    using C = Cfg<BITS, T>;
+    using C = Cfg<BITS, T, PAIR>;
+    auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_gemm_kernel<BITS, T, SETS>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              C::kSmemBytes);
         if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
         configured[dev] = true;
     }
     CUtensorMap tx, tw;
     qmm_status s = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)w.k,
-                               (uint64_t)m, (uint64_t)w.k * 2, kBK, T,
+                               (uint64_t)m, (uint64_t)w.k * 2, kBK, C::kXRows,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != QMM_OK) return s;
     const uint64_t words = (uint64_t)w.k * BITS / 32;
@@ -457,14 +541,28 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.groups = (int32_t)(w.k / w.group);
     p.group_shift = 0;
     while ((1 << p.group_shift) < w.group) ++p.group_shift;
-    p.w_tiles = (int32_t)((w.n + kWRows - 1) / kWRows);
+    constexpr int kTileRows = PAIR ? 2 * kWRows : kWRows;
+    p.w_tiles = (int32_t)((w.n + kTileRows - 1) / kTileRows);
     const int64_t t_tiles = (m + T - 1) / T;
     p.num_tiles = (int32_t)(p.w_tiles * t_tiles);
     p.err = device_error_word();
-    const int grid = (int)std::min<int64_t>(p.num_tiles, sm_count());
-    qmm_gemm_kernel<BITS, T, SETS><<<grid, Warps<SETS>::kThreads, C::kSmemBytes, st>>>(tx, tw, p);
+    const int ctas = PAIR ? 2 : 1;
+    const int units = (int)std::min<int64_t>(p.num_tiles, sm_count() / ctas);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(units * ctas, 1, 1);
+    cfg.blockDim = dim3(Warps<SETS, HALVES>::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ctas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, p);
     count_launch();
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "gemm launch");
 }
 
@@ -480,17 +578,18 @@ bool gemm_supported(const qmm_weight &w) {
 }
 
 qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
-                       uint16_t *y, cudaStream_t st) {
+                       uint16_t *y, bool pair, cudaStream_t st) {
     if (m > (int64_t)INT32_MAX - 256) return fail(QMM_ERR_UNSUPPORTED, "gemm: m too large");
-    static const int sets = [] {
-        const char *e = getenv("QMM_GEMM_SETS");
-        return (e && atoi(e) == 2) ? 2 : 4;
-    }();
+    // Token tile 192 (two 192-column accumulators + four A slots fill TMEM);
+    // four dequantization warp sets of full rows.  CTA pairs (cta_group::2)
+    // on request: they halve the x traffic per SM but lengthen the A-slot
+    // hand-off by a cross-SM round trip, which measured slower on B200.
+    pair = pair && w.n > gemm::kWRows;
     if (w.bits == 4)
-        return sets == 2 ? gemm::launch_t<4, 192, 2>(w, x, m, ep, y, st)
-                         : gemm::launch_t<4, 192, 4>(w, x, m, ep, y, st);
-    return sets == 2 ? gemm::launch_t<8, 192, 2>(w, x, m, ep, y, st)
-                     : gemm::launch_t<8, 192, 4>(w, x, m, ep, y, st);
+        return pair ? gemm::launch_t<4, 192, 4, 1, true>(w, x, m, ep, y, st)
+                    : gemm::launch_t<4, 192, 4, 1, false>(w, x, m, ep, y, st);
+    return pair ? gemm::launch_t<8, 192, 4, 1, true>(w, x, m, ep, y, st)
+                : gemm::launch_t<8, 192, 4, 1, false>(w, x, m, ep, y, st);
 }
 
 }  // namespace qmm

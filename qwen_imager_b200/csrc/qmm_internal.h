@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/qmm.h"
+#include "qmm.h"
 
 namespace qmm {
 
@@ -31,9 +31,14 @@ bool gemv_supported(const qmm_weight &w, int64_t m);
 qmm_status launch_gemv(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
                        uint16_t *y, cudaStream_t st);
 
+// Streaming (bulk-copy) GEMV for m <= 16.
+bool gemv_tma_supported(const qmm_weight &w, int64_t m);
+qmm_status launch_gemv_tma(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
+                           uint16_t *y, cudaStream_t st);
+
 // True when the tcgen05 GEMM supports this layout.
 bool gemm_supported(const qmm_weight &w);
 qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
-                       uint16_t *y, cudaStream_t st);
+                       uint16_t *y, bool pair, cudaStream_t st);
 
 }  // namespace qmm

@@ -55,13 +55,14 @@ def test_fused_linear_matches_oracle(oracle, m, k, n, bits):
     assert mx < MAX_REL and mean < MEAN_REL, (mx, mean)
 
 
+@pytest.mark.parametrize("path", [_lib.QMM_PATH_GEMM, _lib.QMM_PATH_GEMM_PAIR])
 @pytest.mark.parametrize("m,k,n", REFERENCE_SHAPES)
 @pytest.mark.parametrize("bits", [4, 8])
-def test_gemm_consumes_exact_bf16_weights(oracle, m, k, n, bits):
+def test_gemm_consumes_exact_bf16_weights(oracle, m, k, n, bits, path):
     packed, scales, offsets, bias = random_layer(n, k, bits, 64, seed=7 * m + n + bits, bias=True)
     lin = make_linear(packed, scales, offsets, bias, bits, 64)
     x = sin_input(m, k)
-    got = run(lin, x, path=_lib.QMM_PATH_GEMM)
+    got = run(lin, x, path=path)
     assert_one_rounding(got, bf16_weight_reference(oracle, x, packed, scales, offsets, bias, bits, 64), oracle)
 
 
@@ -74,6 +75,8 @@ def test_gemm_identity_probe_reproduces_every_weight(oracle, bits, group, n, k):
     lin = make_linear(packed, scales, offsets, bias, bits, group)
     eye = torch.eye(k, dtype=torch.bfloat16, device="cuda")
     got = from_dev_bf16(lin.forward_fused(eye, path=_lib.QMM_PATH_GEMM))
+    got_pair = from_dev_bf16(lin.forward_fused(eye, path=_lib.QMM_PATH_GEMM_PAIR))
+    assert np.array_equal(got_pair, got)
     w = oracle.bf16_to_f32(oracle.dequantize_bf16(packed, scales, offsets, bits, group))
     ref = oracle.f32_to_bf16(w.T + oracle.bf16_to_f32(bias)[None, :])
     assert np.array_equal(got, ref)
@@ -91,14 +94,15 @@ def test_gemv_small_m(oracle, m, bits):
     assert_one_rounding(got, oracle_f32(oracle, x, packed, scales, offsets, bias, bits, 64), oracle)
 
 
+@pytest.mark.parametrize("path", [_lib.QMM_PATH_GEMM, _lib.QMM_PATH_GEMM_PAIR])
 @pytest.mark.parametrize("m", [1, 17, 100, 191, 192, 193, 385])
 @pytest.mark.parametrize("n", [64, 200, 1000])
-def test_gemm_ragged_edges(oracle, m, n):
+def test_gemm_ragged_edges(oracle, m, n, path):
     k, bits = 320, 4
     packed, scales, offsets, bias = random_layer(n, k, bits, 64, seed=m + 31 * n)
     lin = make_linear(packed, scales, offsets, bias, bits, 64)
     x = sin_input(m, k)
-    got = run(lin, x, path=_lib.QMM_PATH_GEMM)
+    got = run(lin, x, path=path)
     assert_one_rounding(got, bf16_weight_reference(oracle, x, packed, scales, offsets, bias, bits, 64), oracle)
 
 
