@@ -1,7 +1,7 @@
 """Benchmark of the MLX affine quantized linear on B200 (one JSON line).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload ffn_up|linear_4bit|ffn_down|adaln_gemv]
+                  [--workload ffn_up|linear_4bit|ffn_down|adaln_gemv|dit_1024_4bit|dit_2048_8bit]
 
 Default workload (`ffn_up`, the configuration the headline metric is quoted
 on): the DiT FFN up projection, x bf16 [4352, 3072] ~ N(0,1) times 8-bit
@@ -14,6 +14,12 @@ than the 126 MB L2) rotate across steps so every step streams from HBM.
 With N > 1 (torchrun, one process per GPU) every rank runs its own batch of
 the same workload (weak scaling: tokens are independent, no data-path
 collective); value is the total over ranks, timed as the max over ranks.
+
+The dit_* workloads time one denoising step of the 60-block dual-stream DiT
+linear stack (qwen_imager_b200/dit_stack.py) in ms, tensor-parallel over the
+N ranks (strong scaling: the image is fixed, every rank holds 1/N of the
+weights, two NCCL all-reduces of the joint hidden state per block), with a
+breakdown into quantized linears, attention, all-reduce and the rest.
 
 --impl reference times the reference's CPU path for the same workload on the
 host cores (the oracle's restatement: per-call f32 dequantization plus an f32
@@ -42,20 +48,31 @@ WORKLOADS = {
                  [(4352, 12288, 3072, 4, {"residual": True, "gelu_input": True})], 2),
     "adaln_gemv": ("adaLN GEMV 4-bit [1x3072]x[18432x3072]^T", [(1, 3072, 18432, 4, {"silu_input": True})], 1),
 }
+STACK_WORKLOADS = {
+    "dit_1024_4bit": "60-block dual-stream DiT linear stack, 1024x1024 (4096 image + 256 text tokens), 4-bit",
+    "dit_2048_8bit": "60-block dual-stream DiT linear stack, 2048x2048 (16384 image + 512 text tokens), 8-bit",
+}
 ROTATE = 3
 METRIC = "qmm TFLOP/s (quantized DiT linears, bf16 tensor cores)"
+STACK_METRIC = "DiT-stack step ms (60 blocks: quantized linears + joint attention + TP all-reduce)"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=None, help="default 300 (kernels), 5 (dit stacks)")
+    p.add_argument("--warmup", type=int, default=None, help="default 5 (kernels), 3 (dit stacks)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="ffn_up")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(STACK_WORKLOADS), default="ffn_up")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    return p.parse_args()
+    a = p.parse_args()
+    stack = a.workload in STACK_WORKLOADS
+    if a.steps is None:
+        a.steps = 5 if stack else 300
+    if a.warmup is None:
+        a.warmup = 3 if stack else 5
+    return a
 
 
 def step_flops(layers):
@@ -118,7 +135,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.02)
+            self._stop.wait(0.005)
 
     def __enter__(self):
         if self.nv:
@@ -176,13 +193,10 @@ def run_ours(args, rank, world, device):
     if dist:
         import torch.distributed as tdist
 
-    def step(i, ev=None):
+    def step(i, only=None):
         for li, (lin, x, res, y) in enumerate(sets[i % ROTATE]):
-            if ev is not None:
-                ev[li][0].record()
-            lin.forward_fused(x, residual=res, out=y)
-            if ev is not None:
-                ev[li][1].record()
+            if only is None or only == li:
+                lin.forward_fused(x, residual=res, out=y)
 
     for i in range(max(args.warmup, 3)):
         step(i)
@@ -190,26 +204,58 @@ def run_ours(args, rank, world, device):
     if device_error(device):
         raise RuntimeError("device-side wait expired during warm-up")
 
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in layers]
-           for _ in range(args.steps)]
+    # Each rotation set's step is captured once as a CUDA graph (the steady
+    # state of a serving loop: no per-call host work), and each layer alone
+    # as a graph for its per-launch time.
+    cap = torch.cuda.Stream(device)
+    step_graphs, layer_graphs = [], []
+    launches_per_step = None
+    with torch.cuda.stream(cap):
+        for r in range(ROTATE):
+            g = torch.cuda.CUDAGraph()
+            c0 = _lib.launch_count()
+            with torch.cuda.graph(g, stream=cap):
+                step(r)
+            if launches_per_step is None:
+                launches_per_step = _lib.launch_count() - c0
+            step_graphs.append(g)
+            per = []
+            for li in range(len(layers)):
+                gl = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gl, stream=cap):
+                    step(r, only=li)
+                per.append(gl)
+            layer_graphs.append(per)
+    torch.cuda.synchronize()
+    for r in range(ROTATE):
+        step_graphs[r].replay()
+    torch.cuda.synchronize()
+
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(torch.cuda.current_device())
     if dist:
         tdist.barrier()
     torch.cuda.synchronize()
-    launches0 = _lib.launch_count()
     with sampler:
         t0.record()
         for i in range(args.steps):
-            step(i, evs[i])
+            step_graphs[i % ROTATE].replay()
         t1.record()
         torch.cuda.synchronize()
-    launches = _lib.launch_count() - launches0
+    launches = launches_per_step * args.steps
+    elapsed = t0.elapsed_time(t1)
+    # Per-layer launch time, same rotation, on the same stream.
+    kernel_ms = []
+    for li in range(len(layers)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(args.steps):
+            layer_graphs[i % ROTATE][li].replay()
+        b.record()
+        torch.cuda.synchronize()
+        kernel_ms.append(a.elapsed_time(b) / args.steps)
     if dist:
         tdist.barrier()
-    elapsed = t0.elapsed_time(t1)
-    kernel_ms = [sum(e[li][0].elapsed_time(e[li][1]) for e in evs) / args.steps for li in range(len(layers))]
-    if dist:
         t = torch.tensor([elapsed], device=device, dtype=torch.float64)
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         elapsed = float(t.item())
@@ -291,10 +337,174 @@ def run_ours(args, rank, world, device):
         else:
             entry["TFLOP/s"] = round(2.0 * m * n * k / (kernel_ms[li] * 1e-3) / 1e12, 1)
         per_layer.append(entry)
+    del step_graphs, layer_graphs
     return {
         "value": round(value, 3), "ms_per_step": round(ms_per_step, 5), "e2e": e2e, "roofline": roof,
         "gpu_launches": int(launches), "layers": per_layer, "clocks": sampler.summary(),
     }
+
+
+# --------------------------------------------------------------- DiT stack arm
+def run_stack(args, rank, world, device):
+    import torch
+
+    from qwen_imager_b200 import _lib, device_error
+    from qwen_imager_b200.dit_stack import STACKS, DitStack, TensorParallel, Timers
+
+    cfg = STACKS[args.workload]
+    tp = TensorParallel(rank, world)
+    stack = DitStack.random(cfg, tp, seed=1, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(1234)  # the same hidden state and timestep on every rank
+    x0 = torch.randn((cfg.tokens, cfg.hidden), generator=g, device=device).to(torch.bfloat16)
+    temb = torch.randn((cfg.hidden,), generator=g, device=device).to(torch.bfloat16)
+    x = torch.empty_like(x0)
+    dist = world > 1
+    if dist:
+        import torch.distributed as tdist
+
+    def step(timers=None):
+        x.copy_(x0)
+        stack.forward(x, temb, timers)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if device_error(device):
+        raise RuntimeError("device-side wait expired during warm-up")
+    if not torch.isfinite(x.float()).all():
+        raise RuntimeError("non-finite hidden state after one step")
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device())
+    if dist:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    with sampler:
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    elapsed = t0.elapsed_time(t1)
+    if dist:
+        t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    ms = elapsed / args.steps
+
+    # One more step with CUDA events around every op category.
+    timers = Timers(enabled=True)
+    if dist:
+        tdist.barrier()
+    step(timers)
+    torch.cuda.synchronize()
+    parts = {k: round(v, 3) for k, v in timers.totals_ms().items()}
+    lin_flops = cfg.blocks * cfg.linear_flops_per_block()
+    att_flops = cfg.blocks * cfg.attention_flops_per_block()
+    lin_ms = parts.get("linear", float("nan"))
+    peak_tf, _hbm, peak_kind = measured_peaks()
+    achieved = lin_flops / world / (lin_ms * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tf, 4), "traffic": None,
+            "kernel": "all quantized linears of one step on rank 0 (GEMMs + modulation GEMVs)",
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback"}
+
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(x0.shape, dtype=x0.dtype, pin_memory=True)
+        hx.copy_(x0)
+        ht = torch.empty(temb.shape, dtype=temb.dtype, pin_memory=True)
+        ht.copy_(temb)
+        hy = torch.empty(x0.shape, dtype=x0.dtype, pin_memory=True)
+        tt = torch.empty_like(temb)
+
+        def e2e_step():
+            x.copy_(hx, non_blocking=True)
+            tt.copy_(ht, non_blocking=True)
+            stack.forward(x, tt)
+            hy.copy_(x, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if dist:
+            tdist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(2, min(args.steps, 5))
+        a.record()
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record()
+        torch.cuda.synchronize()
+        e_ms = a.elapsed_time(b) / n_e2e
+        if dist:
+            t = torch.tensor([e_ms], device=device, dtype=torch.float64)
+            tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": round(e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(hx.numel() * 2 + ht.numel() * 2),
+               "d2h_bytes_per_step": int(hy.numel() * 2)}
+    if device_error(device):
+        raise RuntimeError("device-side wait expired during the timed region")
+    breakdown = {"ms_" + k: v for k, v in parts.items()}
+    breakdown.update({
+        "linear_tflops_per_rank": round(achieved, 1),
+        "attention_tflops_per_rank": round(att_flops / world / (parts.get("attention", float("nan")) * 1e-3) / 1e12, 1),
+        "linear_tflop_per_step": round(lin_flops / 1e12, 2), "attention_tflop_per_step": round(att_flops / 1e12, 2),
+    })
+    return {"value": round(ms, 3), "ms_per_step": round(ms, 3), "e2e": e2e, "roofline": roof,
+            "gpu_launches": int(launches), "breakdown": breakdown, "clocks": sampler.summary()}
+
+
+def cpu_stack_reference(workload, steps):
+    """The reference CPU path for one block of the stack (every weight of both
+    streams dequantized to f32 per call, f32 GEMMs on a row sample scaled to
+    all rows, f32 attention of a query-row sample against all keys), times 60."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+    from qwen_imager_b200.dit_stack import STACKS
+
+    O.build()
+    cfg = STACKS[workload]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    O.lib().oracle_set_threads(threads)
+    rng = np.random.default_rng(7)
+    h, f, d = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim
+    shapes = [(cfg.mod_features, h, 1), (3 * d, h, None), (h, d, None), (f, h, None), (h, f, None)]
+    layers = []
+    for n, k, m in shapes:
+        w = rng.standard_normal((n, k), dtype=np.float32) * 0.02
+        layers.append((m, k) + O.quantize_affine(w, cfg.bits, 64))
+    rows = CPU_SAMPLE_ROWS
+    times = []
+    for _ in range(steps):
+        t_block = 0.0
+        for stream_tokens in (cfg.img_tokens, cfg.txt_tokens):
+            for (m, k, packed, scales, biases) in layers:
+                m = stream_tokens if m is None else m
+                r = min(rows, m)
+                x = O.f32_to_bf16(rng.standard_normal((r, k), dtype=np.float32))
+                t0 = time.perf_counter()
+                wf = O.dequantize_f32(packed, scales, biases, cfg.bits, 64)
+                t1 = time.perf_counter()
+                y = torch.from_numpy(O.bf16_to_f32(x)) @ torch.from_numpy(wf).T
+                O.f32_to_bf16(y.numpy())
+                t2 = time.perf_counter()
+                t_block += (t1 - t0) + (t2 - t1) * (m / r)
+        q = torch.randn((cfg.heads, rows, cfg.head_dim))
+        kv = torch.randn((2, cfg.heads, cfg.tokens, cfg.head_dim))
+        t0 = time.perf_counter()
+        torch.nn.functional.scaled_dot_product_attention(q, kv[0], kv[1])
+        t_block += (time.perf_counter() - t0) * (cfg.tokens / rows)
+        times.append(t_block * cfg.blocks)
+    t = statistics.median(times)
+    sample = (f"one block timed, x{cfg.blocks} blocks: both streams' weights dequantized to f32 in full "
+              f"(as the reference does per call), f32 GEMMs and f32 attention on {rows}-row samples scaled "
+              f"linearly to all rows; median of {steps}")
+    return t * 1e3, threads, sample
 
 
 # --------------------------------------------------------------------- CPU arm
@@ -347,11 +557,14 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload in STACK_WORKLOADS:
+        return main_stack(args, world, rank, local)
     desc, layers, seed = WORKLOADS[args.workload]
     config = {"workload": f"{args.workload}: {desc}", "global_batch": world,
               "tokens_per_rank": max(l[0] for l in layers), "group": 64,
               "parallelism": f"dp{world} (independent token batches)",
-              "l2": f"{ROTATE} rotating weight/input sets larger than L2 (no flush)"}
+              "l2": f"{ROTATE} rotating weight/input sets larger than L2 (no flush)",
+              "launch": "each step replayed as a CUDA graph; e2e through the eager public API"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -401,6 +614,56 @@ def main():
     if world > 1:
         import torch.distributed as tdist
         tdist.destroy_process_group()
+
+
+def main_stack(args, world, rank, local):
+    from qwen_imager_b200.dit_stack import STACKS
+    cfg = STACKS[args.workload]
+    config = {"workload": f"{args.workload}: {STACK_WORKLOADS[args.workload]}", "global_batch": 1,
+              "tokens": cfg.tokens, "hidden": cfg.hidden, "blocks": cfg.blocks, "bits": cfg.bits, "group": cfg.group,
+              "parallelism": f"tp{world} (column-parallel QKV/up, row-parallel out/down, NCCL all-reduce)",
+              "l2": "weights of every step (GBs) far exceed L2 (no flush)"}
+    common = {"metric": STACK_METRIC, "unit": "ms", "steps": args.steps, "warmup": args.warmup,
+              "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "config": config}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ms, cores, sample = cpu_stack_reference(args.workload, max(1, min(args.steps, 2)))
+        out = dict(common, value=round(ms, 1), impl="reference", n_gpus=args.gpus, ms_per_step=round(ms, 1),
+                   dtype="f32", data="synthetic",
+                   cpu_baseline={"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+                   e2e={"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(out), flush=True)
+        return
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=180))
+    try:
+        res = run_stack(args, rank, world, device)
+        out = dict(common, value=res["value"], n_gpus=world, ms_per_step=res["ms_per_step"], dtype="bf16",
+                   data="synthetic (random 4/8-bit codes with N(0,0.02)-sized scales; random hidden state)",
+                   e2e=res["e2e"], roofline=res["roofline"], gpu_launches=res["gpu_launches"],
+                   clocks=res["clocks"], breakdown=res["breakdown"])
+        if rank == 0 and world == 1 and not args.no_cpu:
+            try:
+                ms, cores, sample = cpu_stack_reference(args.workload, 1)
+                out["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port",
+                                       "sample": sample}
+            except Exception as exc:
+                out["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as tdist
+            tdist.barrier()
+            tdist.destroy_process_group()
 
 
 if __name__ == "__main__":

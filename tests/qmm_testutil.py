@@ -68,3 +68,31 @@ def assert_one_rounding(got, ref_f32, oracle=O):
     bad = (ulps > 1) & (d > tol)
     assert not bad.any(), (int(ulps.max()), float(d[bad].max() / np.abs(ref_f32).max()))
     assert (ulps > 0).mean() < 0.05
+
+
+def _bits16(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _bits32(t):
+    return t.detach().cpu().contiguous().view(torch.int32).numpy().view(np.uint32)
+
+
+_ACT_CODES = {None: 0, "none": 0, "gelu_tanh": 1, "silu": 2}
+
+
+def oracle_run_linear(lin, x, *, gate=None, residual=None, activation=None, out=None):
+    """The oracle's fused linear on CPU tensors, with the same signature as the
+    stack's CUDA linear: residual + gate * act(x . W^T + bias), rounded once."""
+    a = lin.affine
+    m = x.numel() // a.input
+    y = O.linear_f32(_bits16(x.reshape(m, a.input)), _bits32(a.packed), _bits16(a.scales),
+                     _bits16(a.offsets), a.bits, a.group, None if a.bias is None else _bits16(a.bias))
+    r = O.epilogue_bf16(y, None if gate is None else _bits16(gate.reshape(-1)),
+                        None if residual is None else _bits16(residual.reshape(m, a.output)),
+                        _ACT_CODES[activation])
+    t = torch.from_numpy(r.view(np.int16)).view(torch.bfloat16).reshape(m, a.output)
+    if out is None:
+        return t
+    out.copy_(t.reshape(out.shape))
+    return out

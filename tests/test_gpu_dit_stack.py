@@ -1,0 +1,82 @@
+"""The tensor-parallel DiT linear stack on B200: CUDA linears against the
+oracle's linears on CPU, and (with two GPUs) NCCL tensor parallelism against
+one rank."""
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from qwen_imager_b200.dit_stack import DitStack, StackConfig, TensorParallel, stream_weights_full
+from qwen_imager_b200.quant import Affine
+from qmm_testutil import _bits16, oracle_run_linear, rel_errors
+
+pytestmark = pytest.mark.gpu
+
+SMALL = StackConfig(img_tokens=320, txt_tokens=64, bits=4, blocks=2, hidden=512, heads=4, head_dim=128,
+                    ffn=1024)
+SMALL8 = StackConfig(img_tokens=200, txt_tokens=56, bits=8, blocks=2, hidden=512, heads=4, head_dim=128,
+                     ffn=1024)
+
+
+def _to(a: Affine, device) -> Affine:
+    return Affine(packed=a.packed.to(device), scales=a.scales.to(device), offsets=a.offsets.to(device),
+                  bias=None if a.bias is None else a.bias.to(device), bits=a.bits, group=a.group, input=a.input)
+
+
+def _weights(cfg, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    full = [[stream_weights_full(cfg, g, "cpu") for _ in range(2)] for _ in range(cfg.blocks)]
+    return [[{k: _to(v, device) for k, v in f.items()} for f in blk] for blk in full]
+
+
+def _inputs(cfg, seed):
+    g = torch.Generator().manual_seed(seed + 1)
+    return (torch.randn((cfg.tokens, cfg.hidden), generator=g).to(torch.bfloat16),
+            torch.randn((cfg.hidden,), generator=g).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("cfg", [SMALL, SMALL8], ids=["4bit", "8bit"])
+def test_stack_cuda_matches_oracle_stack(cfg):
+    seed = 21
+    x, temb = _inputs(cfg, seed)
+    ref = DitStack.from_full(cfg, _weights(cfg, seed, "cpu"), TensorParallel(),
+                             run_linear=oracle_run_linear).forward(x.clone(), temb)
+    got = DitStack.from_full(cfg, _weights(cfg, seed, "cuda"), TensorParallel()).forward(x.cuda(), temb.cuda())
+    mx, mean = rel_errors(_bits16(got), ref.float().numpy())
+    assert mx <= 1e-2 and mean <= 1e-3, (mx, mean)
+
+
+def _nccl_rank(rank, world, port, seed, path):
+    import datetime
+
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        x, temb = _inputs(SMALL, seed)
+        dev = torch.device("cuda", rank)
+        stack = DitStack.from_full(SMALL, _weights(SMALL, seed, dev), TensorParallel(rank, world))
+        y = stack.forward(x.to(dev), temb.to(dev))
+        torch.cuda.synchronize()
+        torch.save(y.cpu(), f"{path}.{rank}")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_stack_two_rank_nccl_matches_one_rank(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    seed = 23
+    x, temb = _inputs(SMALL, seed)
+    ref = DitStack.from_full(SMALL, _weights(SMALL, seed, "cuda"), TensorParallel()).forward(x.cuda(), temb.cuda())
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    path = str(tmp_path / "y")
+    mp.start_processes(_nccl_rank, args=(2, port, seed, path), nprocs=2, start_method="spawn")
+    for r in range(2):
+        mx, mean = rel_errors(_bits16(torch.load(f"{path}.{r}")), ref.float().cpu().numpy())
+        assert mx <= 1e-2 and mean <= 1e-3, (r, mx, mean)
