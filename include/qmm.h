@@ -96,7 +96,8 @@ typedef struct qmm_epilogue {
 /* Kernel selection for qmm_linear_ex (tests and benchmarks). */
 typedef enum qmm_path {
     QMM_PATH_AUTO = 0,   /* m <= 16: GEMV, otherwise the tcgen05 GEMM */
-    QMM_PATH_GEMV = 1,   /* warp-per-row streaming kernel, any m (slow for large m) */
+    QMM_PATH_GEMV = 1,   /* streaming GEMVs: tensor-core (4-bit, m <= 16), FMA (m <= 16),
+                            warp-per-row (any m, slow for large m), first that fits */
     QMM_PATH_GEMM = 2,   /* tcgen05/TMEM GEMM, any m >= 1 */
     QMM_PATH_GEMM_PAIR = 3  /* the GEMM on CTA pairs (cta_group::2, MMA M = 256) */
 } qmm_path;
@@ -146,11 +147,13 @@ QMM_API qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t
 
 /*
  * Reads and clears the device-side error word that bounded waits inside the
- * GEMM set when they expire (0 = none).  Synchronizes `stream`.
+ * kernels set when they expire (0 = none).  Synchronizes `stream`.  No
+ * counterpart in quant.rs (Metal has no bounded waits to report).
  */
 QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
 
-/* Number of kernels this library has launched in the calling process. */
+/* Number of kernels this library has launched in the calling process (kernels
+ * captured into a CUDA graph count once, at capture).  No counterpart in quant.rs. */
 QMM_API uint64_t qmm_launch_count(void);
 
 #ifdef __cplusplus

@@ -169,9 +169,12 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
     if ((s = check_device()) != QMM_OK) return s;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (path == QMM_PATH_AUTO)
-        path = (m <= 16 && (qmm::gemv_tma_supported(*w, m) || qmm::gemv_supported(*w, m))) ? QMM_PATH_GEMV
-                                                                                           : QMM_PATH_GEMM;
+        path = (m <= 16 && (qmm::gemv_mma_supported(*w, m) || qmm::gemv_tma_supported(*w, m) ||
+                            qmm::gemv_supported(*w, m)))
+                   ? QMM_PATH_GEMV
+                   : QMM_PATH_GEMM;
     if (path == QMM_PATH_GEMV) {
+        if (qmm::gemv_mma_supported(*w, m)) return qmm::launch_gemv_mma(*w, x, m, e, y, st);
         if (qmm::gemv_tma_supported(*w, m)) return qmm::launch_gemv_tma(*w, x, m, e, y, st);
         if (!qmm::gemv_supported(*w, m))
             return fail(QMM_ERR_UNSUPPORTED,

@@ -47,6 +47,16 @@ __device__ __forceinline__ float epilogue_value(const EpilogueArgs &e, const Fea
     return t;
 }
 
+// Same as epilogue_value with the residual element already loaded (`resid`
+// is ignored when the epilogue has no residual).
+__device__ __forceinline__ float epilogue_value_rv(const EpilogueArgs &e, const FeatureConsts &c,
+                                                   float acc, float resid) {
+    float t = apply_activation(acc + c.bias, e.act);
+    if (e.gate) t = t * c.gate;
+    if (e.residual) t = resid + t;
+    return t;
+}
+
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
     __nv_bfloat16 b = __float2bfloat16_rn(v);
     return *reinterpret_cast<uint16_t *>(&b);

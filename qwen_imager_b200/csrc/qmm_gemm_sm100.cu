@@ -437,15 +437,26 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     if (lane == 0) arrive_leader(&acc_empty[b]);
                 }
                 if (nvalid) {
+                    // Residual values of 8 tokens are loaded before any of
+                    // their outputs is stored: y may alias the residual, so
+                    // interleaved load/store pairs would serialize on memory
+                    // latency.  Each thread reads only elements it writes.
+                    const int64_t mrow = m0 + c0;
+                    const int lim = (int)(p.m - mrow < 32 ? p.m - mrow : 32);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int64_t mm = m0 + c0 + j;
-                        if (mm < p.m) {
-                            const int64_t idx = mm * p.n + n;
-                            const float val = epilogue_value(
-                                p.ep, fc, __uint_as_float(v[j]),
-                                p.ep.residual ? p.ep.residual + idx : nullptr);
-                            p.y[idx] = f32_to_bf16_bits(val);
+                    for (int h = 0; h < 32; h += 8) {
+                        float rv[8];
+                        if (p.ep.residual) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                rv[j] = h + j < lim ? bf16_bits_to_f32(p.ep.residual[(mrow + h + j) * p.n + n]) : 0.0f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            if (h + j < lim) {
+                                const float val = epilogue_value_rv(p.ep, fc, __uint_as_float(v[h + j]), rv[j]);
+                                p.y[(mrow + h + j) * p.n + n] = f32_to_bf16_bits(val);
+                            }
                         }
                     }
                 }

@@ -31,6 +31,11 @@ bool gemv_supported(const qmm_weight &w, int64_t m);
 qmm_status launch_gemv(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
                        uint16_t *y, cudaStream_t st);
 
+// Tensor-core (mma.sync) streaming GEMV: 4-bit, m <= 16, group a multiple of 64.
+bool gemv_mma_supported(const qmm_weight &w, int64_t m);
+qmm_status launch_gemv_mma(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
+                           uint16_t *y, cudaStream_t st);
+
 // Streaming (bulk-copy) GEMV for m <= 16.
 bool gemv_tma_supported(const qmm_weight &w, int64_t m);
 qmm_status launch_gemv_tma(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,

@@ -106,7 +106,9 @@ def _slice_affine(a: Affine, rows: Optional[torch.Tensor] = None, k0: int = 0, k
     offsets = a.offsets[:, k0 // a.group:k1 // a.group]
     bias = a.bias if keep_bias else None
     if rows is not None:
-        packed, scales, offsets = packed[rows], scales[rows], offsets[rows]
+        # (index_select has no uint32 kernel on CUDA: gather the words as int32)
+        packed = packed.view(torch.int32)[rows].view(torch.uint32)
+        scales, offsets = scales[rows], offsets[rows]
         bias = None if bias is None else bias[rows]
     return Affine(packed=packed.contiguous(), scales=scales.contiguous(), offsets=offsets.contiguous(),
                   bias=None if bias is None else bias.contiguous(), bits=a.bits, group=a.group,
