@@ -6,7 +6,10 @@
 // One persistent CTA per SM.  A producer warp streams blocks of RB weight
 // rows (codes with one bulk copy per row into a bank-staggered row stride,
 // plus the block's scales and offsets) into a ring of shared-memory stages.
-// Sixteen consumer warps split a block into 16-row tiles x K slices.
+// Consumer warps split a block into tile groups x K slices and leave
+// per-slice partial sums in a double buffer; a reducer warp
+// sums the slices, applies the epilogue and stores y, so consumer warps never
+// wait for one another.
 //
 // Arithmetic.  Per 64-code unit u of a row (inside one quantization group),
 //   sum_k x_k (s q_k + o) = s * D_u + (o - 128 s) * X_u,
@@ -33,8 +36,16 @@
 namespace qmm {
 namespace gemvtc {
 
-constexpr int kConsumerWarps = 16;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+// CW consumer warps (16: measured faster than 24 single-tile warps, because
+// two tiles per warp share their x fragments), then the producer warp and the
+// reducer warp (at most 32 warps per block).
+template <int CW>
+struct Warps {
+    static_assert(CW + 2 <= 32, "at most 1024 threads per block");
+    static constexpr int kProducer = CW;
+    static constexpr int kReducer = CW + 1;
+    static constexpr int kThreads = (CW + 2) * 32;
+};
 constexpr int kMaxStages = 4;
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr int kUnit = 64;  // codes per four-MMA unit
@@ -73,12 +84,13 @@ __device__ __forceinline__ uint32_t code_pair(uint32_t nibbles) {
 
 // Shared memory (16-byte aligned regions):
 //   stages [stages][rb * row_stride codes | rb*groups scales | rb*groups offsets]
-//   xp     [m][units][4 lanes t][4 MMAs j][2] u32   x in MMA order, bf16 pairs
+//   xp     [m + 1][units][4 lanes t][4 MMAs j][2] u32   x in MMA order (bf16 pairs); row m zero
 //   xsum   [units][MP] f32                            X_u per token (zero beyond m)
-//   part   [2][ks][rb][m] f32                         partial sums per K slice
-//   bars   full[kMaxStages], empty[kMaxStages]
-template <int MT>
-__global__ void __launch_bounds__(kThreads, 1) qmm_gemv_mma_kernel(const Params p) {
+//   part   [2][ks][rb][m] f32                         partial sums per K slice (ks = 16 warps)
+//   bars   full[kMaxStages], empty[kMaxStages], pready[2], pfree[2]
+template <int MT, int TPW, int CW>
+__global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(const Params p) {
+    using W = Warps<CW>;
     constexpr int MP = 8 * MT;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *stages = smem;
@@ -88,18 +100,52 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_mma_kernel(const Params 
     uint64_t *full = reinterpret_cast<uint64_t *>(
         (reinterpret_cast<uintptr_t>(part + 2 * (size_t)p.ks * p.rb * p.m) + 15) & ~uintptr_t(15));
     uint64_t *empty = full + kMaxStages;
+    uint64_t *pready = empty + kMaxStages;  // [2] consumer warps -> reducer
+    uint64_t *pfree = pready + 2;           // [2] reducer -> consumer warps
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], CW);
+        }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&pready[q], CW);
+            mbar_init(&pfree[q], 1);
         }
         fence_barrier_init();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == W::kReducer) {
+        // ----------------------------------------------------------- reducer
+        // Block j's partials are in part[j & 1]; the (j >> 1)-th completion of
+        // pready[j & 1] says every consumer warp has written its slice.
+        bool rok = true;
+        int j = 0;
+        for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
+            const int q = j & 1;
+            rok = rok && mbar_wait(&pready[q], (j >> 1) & 1, p.err, kErrTimeoutEpilogue);
+            const int64_t row0 = (int64_t)b * p.rb;
+            const float *pr = part + (size_t)q * p.ks * p.rb * p.m;
+            for (int i = lane; rok && i < p.rb * p.m; i += 32) {
+                const int row = i / p.m, tok = i - row * p.m;
+                const int64_t n = row0 + row;
+                if (n >= p.n) continue;
+                float v = 0.0f;
+#pragma unroll 4
+                for (int ks = 0; ks < p.ks; ++ks) v += pr[(size_t)ks * p.rb * p.m + i];
+                const FeatureConsts fc = load_feature_consts(p.ep, n, true);
+                const int64_t idx = (int64_t)tok * p.n + n;
+                p.y[idx] = f32_to_bf16_bits(epilogue_value(p.ep, fc, v, p.ep.residual ? p.ep.residual + idx : nullptr));
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfree[q]);
+        }
+        return;
+    }
+
+    if (warp == W::kProducer) {
         // ---------------------------------------------------------- producer
         int j = 0;
         for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
@@ -126,48 +172,60 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_mma_kernel(const Params 
 
     // ------------------------------------------------- stage x in MMA order
     // Entry (token, u, t, j, r) holds x at codes c0 = 64u + 16t + 8(j/2) +
-    // (j%2) + 4r and c0 + 2 of the token (low half c0).
-    const int consumer_threads = kConsumerWarps * 32;
-    const int per_token = p.units * 32;
-    for (int i = threadIdx.x; i < p.m * per_token; i += consumer_threads) {
-        const int tok = i / per_token, e = i - tok * per_token;
-        const int u = e >> 5, t = (e >> 3) & 3, jj = (e >> 1) & 3, r = e & 1;
-        const int c0 = u * kUnit + 16 * t + 8 * (jj >> 1) + (jj & 1) + 4 * r;
-        const uint16_t *xt = p.x + (size_t)tok * p.k;
-        xp[(size_t)tok * p.xp_stride + e] = (uint32_t)__ldg(xt + c0) | ((uint32_t)__ldg(xt + c0 + 2) << 16);
-    }
-    // X_u: eight lanes per (unit, token), 8 codes each, reduced with shuffles.
-    for (int i = threadIdx.x; i < p.units * MP * 8; i += consumer_threads) {
-        const int c = i & 7, ut = i >> 3;
-        const int u = ut / MP, tok = ut - u * MP;
+    // (j%2) + 4r and c0 + 2 of the token (low half c0).  One task per
+    // (token, u, t) reads its 16 codes with two 16-byte loads and writes its 8
+    // entries; the four tasks of a unit sum X_u with shuffles.  Token row m of
+    // xp is zero: B fragments of lanes whose token is >= m read it.
+    const int consumer_threads = CW * 32;
+    for (int i = threadIdx.x; i < p.units * 32; i += consumer_threads) xp[(size_t)p.m * p.xp_stride + i] = 0u;
+    for (int i = threadIdx.x; i < p.units * MP; i += consumer_threads)
+        if (i % MP >= p.m) xsum[i] = 0.0f;
+    const int tasks = p.m * p.units * 4;
+    const int tasks_rounded = (tasks + 31) & ~31;  // whole warps: the shuffles below see all lanes
+    for (int base = 0; base < tasks_rounded; base += consumer_threads) {
+        const int i = base + (int)threadIdx.x;
+        const bool act = i < tasks;
+        const int t = i & 3, ut = i >> 2;
+        const int tok = act ? ut / p.units : 0, u = act ? ut - tok * p.units : 0;
         float sum = 0.0f;
-        if (tok < p.m) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)tok * p.k + u * kUnit) + c);
-            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        if (act) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.x + (size_t)tok * p.k + u * kUnit + 16 * t);
+            const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+            const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};  // codes 2i | 2i+1
+            uint32_t out[8];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+            for (int e = 0; e < 8; ++e) {
+                const int jj = e >> 1, r = e & 1;
+                const int c0 = 8 * (jj >> 1) + (jj & 1) + 4 * r, c1 = c0 + 2;
+                const uint32_t lo = (w[c0 >> 1] >> ((c0 & 1) * 16)) & 0xFFFFu;
+                const uint32_t hi = (w[c1 >> 1] >> ((c1 & 1) * 16)) & 0xFFFFu;
+                out[e] = lo | (hi << 16);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)tok * p.xp_stride + u * 32 + t * 8);
+            dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+            dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
         }
-        // units * MP * 8 and the stride are multiples of 32: a warp's lanes
-        // are all in the loop or all out of it, so the full-mask shuffles are safe.
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        if (c == 0) xsum[ut] = sum;
+        if (act && t == 0) xsum[u * MP + tok] = sum;
     }
     named_barrier(1, consumer_threads);
 
     // ---------------------------------------------------------- consumers
+    // Warp w takes K slice w % ks (units [slice * upw, (slice + 1) * upw)) of
+    // the TPW 16-row tiles of tile group w / ks; lane (g, t) holds rows
+    // 16 tile + g and 16 tile + g + 8, tokens 2t and 2t + 1 of each 8-token tile.
     const int g = lane >> 2, t = lane & 3;
-    const int rt = warp / p.ks, ksl = warp - rt * p.ks;
-    const int row_a = rt * 16 + g, row_b = row_a + 8;
+    const int tg = warp / p.ks, ksl = warp - tg * p.ks;
+    const int tile0 = tg * TPW;
     const int u0 = ksl * p.upw, u1 = min(p.units, u0 + p.upw);
-    // B fragments: lanes whose token (g, plus 8 per token tile) is >= m use zeros.
     const uint32_t *xb[MT];
-    bool has_tok[MT];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-        has_tok[mt] = mt * 8 + g < p.m;
-        xb[mt] = xp + (size_t)(has_tok[mt] ? mt * 8 + g : 0) * p.xp_stride + t * 8;
+        const int tok = mt * 8 + g;
+        xb[mt] = xp + (size_t)(tok < p.m ? tok : p.m) * p.xp_stride + t * 8;
     }
     bool ok = true;
     int j = 0;
@@ -177,111 +235,113 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_gemv_mma_kernel(const Params 
         const uint8_t *st = stages + (size_t)s * p.stage_bytes;
         const uint16_t *ssc = reinterpret_cast<const uint16_t *>(st + p.meta_off);
         const uint16_t *sof = ssc + (size_t)p.rb * p.groups;
-        float acc[MT][4];
+        float2 acc[MT][TPW][2];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[mt][q] = 0.0f;
+            for (int tl = 0; tl < TPW; ++tl) acc[mt][tl][0] = acc[mt][tl][1] = make_float2(0.0f, 0.0f);
         if (ok) {
-            const uint8_t *ra = st + (size_t)row_a * p.row_stride + t * 8;
-            const uint8_t *rbp = st + (size_t)row_b * p.row_stride + t * 8;
+            const uint8_t *rowp = st + (size_t)(tile0 * 16 + g) * p.row_stride + t * 8;
+            const size_t tile_bytes = (size_t)16 * p.row_stride, half_bytes = (size_t)8 * p.row_stride;
 #pragma unroll 2
             for (int u = u0; u < u1; ++u) {
-                const uint2 wa = *reinterpret_cast<const uint2 *>(ra + u * 32);
-                const uint2 wb = *reinterpret_cast<const uint2 *>(rbp + u * 32);
                 uint32_t bfr[MT][8];
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    if (has_tok[mt]) {
-                        const uint4 v0 = *reinterpret_cast<const uint4 *>(xb[mt] + u * 32);
-                        const uint4 v1 = *reinterpret_cast<const uint4 *>(xb[mt] + u * 32 + 4);
-                        bfr[mt][0] = v0.x; bfr[mt][1] = v0.y; bfr[mt][2] = v0.z; bfr[mt][3] = v0.w;
-                        bfr[mt][4] = v1.x; bfr[mt][5] = v1.y; bfr[mt][6] = v1.z; bfr[mt][7] = v1.w;
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) bfr[mt][q] = 0u;
-                    }
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(xb[mt] + u * 32);
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(xb[mt] + u * 32 + 4);
+                    bfr[mt][0] = v0.x; bfr[mt][1] = v0.y; bfr[mt][2] = v0.z; bfr[mt][3] = v0.w;
+                    bfr[mt][4] = v1.x; bfr[mt][5] = v1.y; bfr[mt][6] = v1.z; bfr[mt][7] = v1.w;
                 }
-                // Two independent accumulator chains (low- and high-nibble MMAs).
-                float d[MT][4], e[MT][4];
+                // Per tile: two independent chains (low- and high-nibble MMAs).
+                float d[MT][TPW][4], e[MT][TPW][4];
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) d[mt][q] = e[mt][q] = 0.0f;
-                const uint32_t wa_[2] = {wa.x, wa.y}, wb_[2] = {wb.x, wb.y};
+                    for (int tl = 0; tl < TPW; ++tl)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {  // word 2t + h of the unit
-                    const uint32_t la = wa_[h] & 0x0F0F0F0Fu, ha = (wa_[h] >> 4) & 0x0F0F0F0Fu;
-                    const uint32_t lb = wb_[h] & 0x0F0F0F0Fu, hb = (wb_[h] >> 4) & 0x0F0F0F0Fu;
+                        for (int q = 0; q < 4; ++q) d[mt][tl][q] = e[mt][tl][q] = 0.0f;
 #pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        // MMA 2h: low nibbles; MMA 2h + 1: high nibbles.
-                        mma_bf16_m16n8k16(d[mt], code_pair<0x4140>(la), code_pair<0x4140>(lb),
-                                          code_pair<0x4342>(la), code_pair<0x4342>(lb), bfr[mt][4 * h + 0],
-                                          bfr[mt][4 * h + 1]);
-                        mma_bf16_m16n8k16(e[mt], code_pair<0x4140>(ha), code_pair<0x4140>(hb),
-                                          code_pair<0x4342>(ha), code_pair<0x4342>(hb), bfr[mt][4 * h + 2],
-                                          bfr[mt][4 * h + 3]);
+                for (int tl = 0; tl < TPW; ++tl) {
+                    const uint2 wa = *reinterpret_cast<const uint2 *>(rowp + tl * tile_bytes + u * 32);
+                    const uint2 wb = *reinterpret_cast<const uint2 *>(rowp + tl * tile_bytes + half_bytes + u * 32);
+                    const uint32_t wa_[2] = {wa.x, wa.y}, wb_[2] = {wb.x, wb.y};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {  // word 2t + h of the unit
+                        const uint32_t la = wa_[h] & 0x0F0F0F0Fu, ha = (wa_[h] >> 4) & 0x0F0F0F0Fu;
+                        const uint32_t lb = wb_[h] & 0x0F0F0F0Fu, hb = (wb_[h] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            // MMA 2h: low nibbles; MMA 2h + 1: high nibbles.
+                            mma_bf16_m16n8k16(d[mt][tl], code_pair<0x4140>(la), code_pair<0x4140>(lb),
+                                              code_pair<0x4342>(la), code_pair<0x4342>(lb), bfr[mt][4 * h + 0],
+                                              bfr[mt][4 * h + 1]);
+                            mma_bf16_m16n8k16(e[mt][tl], code_pair<0x4140>(ha), code_pair<0x4140>(hb),
+                                              code_pair<0x4342>(ha), code_pair<0x4342>(hb), bfr[mt][4 * h + 2],
+                                              bfr[mt][4 * h + 3]);
+                        }
                     }
                 }
                 const int gi = u >> p.unit_shift;
-                const float sa = bf16_bits_to_f32(ssc[row_a * p.groups + gi]);
-                const float sb = bf16_bits_to_f32(ssc[row_b * p.groups + gi]);
-                const float ca = fmaf(-128.0f, sa, bf16_bits_to_f32(sof[row_a * p.groups + gi]));
-                const float cb = fmaf(-128.0f, sb, bf16_bits_to_f32(sof[row_b * p.groups + gi]));
+                float2 sc[TPW][2], cc[TPW][2];
+#pragma unroll
+                for (int tl = 0; tl < TPW; ++tl) {
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int row = (tile0 + tl) * 16 + hr * 8 + g;
+                        const float sv = bf16_bits_to_f32(ssc[row * p.groups + gi]);
+                        const float cv = fmaf(-128.0f, sv, bf16_bits_to_f32(sof[row * p.groups + gi]));
+                        sc[tl][hr] = make_float2(sv, sv);
+                        cc[tl][hr] = make_float2(cv, cv);
+                    }
+                }
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) d[mt][q] += e[mt][q];
                     const float2 xs2 = *reinterpret_cast<const float2 *>(xsum + u * MP + mt * 8 + 2 * t);
-                    acc[mt][0] = fmaf(sa, d[mt][0], fmaf(ca, xs2.x, acc[mt][0]));
-                    acc[mt][1] = fmaf(sa, d[mt][1], fmaf(ca, xs2.y, acc[mt][1]));
-                    acc[mt][2] = fmaf(sb, d[mt][2], fmaf(cb, xs2.x, acc[mt][2]));
-                    acc[mt][3] = fmaf(sb, d[mt][3], fmaf(cb, xs2.y, acc[mt][3]));
+#pragma unroll
+                    for (int tl = 0; tl < TPW; ++tl) {
+                        const float2 da = add_f32x2(make_float2(d[mt][tl][0], d[mt][tl][1]),
+                                                    make_float2(e[mt][tl][0], e[mt][tl][1]));
+                        const float2 db = add_f32x2(make_float2(d[mt][tl][2], d[mt][tl][3]),
+                                                    make_float2(e[mt][tl][2], e[mt][tl][3]));
+                        acc[mt][tl][0] = fma_f32x2(sc[tl][0], da, fma_f32x2(cc[tl][0], xs2, acc[mt][tl][0]));
+                        acc[mt][tl][1] = fma_f32x2(sc[tl][1], db, fma_f32x2(cc[tl][1], xs2, acc[mt][tl][1]));
+                    }
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done reading the stage
-        // Partial sums of this K slice: rows row_a, row_b; tokens mt*8 + 2t, +1.
-        float *pb = part + ((size_t)(j & 1) * p.ks + ksl) * p.rb * p.m;
+        // Partial sums of this K slice into part[j & 1], once the reducer has
+        // finished block j - 2 there.
+        const int q = j & 1;
+        ok = ok && mbar_wait(&pfree[q], ((j >> 1) & 1) ^ 1, p.err, kErrTimeoutDequant);
+        float *pb = part + ((size_t)q * p.ks + ksl) * p.rb * p.m;
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
             const int t0 = mt * 8 + 2 * t;
-            if (t0 < p.m) {
-                pb[row_a * p.m + t0] = acc[mt][0];
-                pb[row_b * p.m + t0] = acc[mt][2];
-            }
-            if (t0 + 1 < p.m) {
-                pb[row_a * p.m + t0 + 1] = acc[mt][1];
-                pb[row_b * p.m + t0 + 1] = acc[mt][3];
+#pragma unroll
+            for (int tl = 0; tl < TPW; ++tl) {
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = (tile0 + tl) * 16 + hr * 8 + g;
+                    if (t0 < p.m) pb[row * p.m + t0] = acc[mt][tl][hr].x;
+                    if (t0 + 1 < p.m) pb[row * p.m + t0 + 1] = acc[mt][tl][hr].y;
+                }
             }
         }
-        named_barrier(1, consumer_threads);
-        // Reduce over K slices, epilogue, store.  (The next block writes the
-        // other half of `part`; the barrier of the block after that orders
-        // these reads before its writes.)
-        const int64_t row0 = (int64_t)b * p.rb;
-        const float *pr = part + (size_t)(j & 1) * p.ks * p.rb * p.m;
-        for (int i = threadIdx.x; i < p.rb * p.m; i += consumer_threads) {
-            const int row = i / p.m, tok = i - row * p.m;
-            const int64_t n = row0 + row;
-            if (!ok || n >= p.n) continue;
-            float v = 0.0f;
-            for (int q = 0; q < p.ks; ++q) v += pr[(size_t)q * p.rb * p.m + i];
-            const FeatureConsts fc = load_feature_consts(p.ep, n, true);
-            const int64_t idx = (int64_t)tok * p.n + n;
-            p.y[idx] = f32_to_bf16_bits(epilogue_value(p.ep, fc, v, p.ep.residual ? p.ep.residual + idx : nullptr));
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pready[q]);
     }
 }
 
 struct Plan {
-    int rb, ks, stages, row_stride, stage_bytes, meta_off, xp_stride;
+    int rb, ks, tpw, cw, stages, row_stride, stage_bytes, meta_off, xp_stride;
     size_t smem;
 };
 
 static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
+    pl.cw = 16;
     const int mt = m <= 8 ? 1 : 2;
     const int64_t units = w.k / kUnit, groups = w.k / w.group;
     const int64_t row_bytes = w.k / 2;
@@ -290,17 +350,21 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     const int64_t r128 = row_bytes % 128;
     pl.row_stride = (int)(r128 == 32 || r128 == 96 ? row_bytes : row_bytes + 32);
     pl.xp_stride = (int)(units * 32 + 4);  // +16 bytes: tokens start in different bank quads
-    const size_t xs = (size_t)m * pl.xp_stride * 4 + (size_t)units * 8 * mt * 4;
+    const size_t xs = (size_t)(m + 1) * pl.xp_stride * 4 + (size_t)units * 8 * mt * 4;
     for (int rb = 32; rb >= 16; rb /= 2) {
-        const int ks = kConsumerWarps / (rb / 16);
+        // 16 warps on a 32-row block: one tile group of two tiles; otherwise
+        // one tile per warp and rb / 16 tile groups.
+        const int tpw = (pl.cw == 16 && rb == 32) ? 2 : 1;
+        const int ks = pl.cw / ((rb / 16) / tpw);
         const int64_t meta = (int64_t)rb * groups * 2;
         const int64_t stage = (int64_t)rb * pl.row_stride + 2 * meta;
-        const size_t fixed = xs + 2 * (size_t)ks * rb * m * 4 + 16 + 2 * kMaxStages * 8 + 64;
+        const size_t fixed = xs + 2 * (size_t)ks * rb * m * 4 + 16 + (2 * kMaxStages + 4) * 8 + 64;
         int stages = kMaxStages;
         while (stages >= 2 && fixed + (size_t)stages * stage > kSmemLimit) --stages;
         if (stages < 2) continue;
         pl.rb = rb;
         pl.ks = ks;
+        pl.tpw = tpw;
         pl.stages = stages;
         pl.stage_bytes = (int)stage;
         pl.meta_off = rb * pl.row_stride;
@@ -310,17 +374,18 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     return false;
 }
 
-template <int MT>
+template <int MT, int TPW, int CW>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
                            uint16_t *y, cudaStream_t st) {
     Plan pl;
-    if (!plan_for(w, m, pl)) return fail(QMM_ERR_UNSUPPORTED, "gemv (mma): layout does not fit shared memory");
+    if (!plan_for(w, m, pl) || pl.tpw != TPW || pl.cw != CW)
+        return fail(QMM_ERR_UNSUPPORTED, "gemv (mma): layout does not fit shared memory");
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_gemv_mma_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(qmm_gemv_mma_kernel<MT, TPW, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemLimit);
         if (e != cudaSuccess) return cuda_fail(e, "gemv (mma) smem attribute");
         configured[dev] = true;
@@ -352,7 +417,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.xp_stride = pl.xp_stride;
     p.err = device_error_word();
     const int grid = (int)std::min<int64_t>(p.nblocks, sm_count());
-    qmm_gemv_mma_kernel<MT><<<grid, kThreads, pl.smem, st>>>(p);
+    qmm_gemv_mma_kernel<MT, TPW, CW><<<grid, Warps<CW>::kThreads, pl.smem, st>>>(p);
     count_launch();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "gemv (mma) launch");
@@ -374,7 +439,11 @@ bool gemv_mma_supported(const qmm_weight &w, int64_t m) {
 
 qmm_status launch_gemv_mma(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
                            uint16_t *y, cudaStream_t st) {
-    return m <= 8 ? gemvtc::launch_t<1>(w, x, m, ep, y, st) : gemvtc::launch_t<2>(w, x, m, ep, y, st);
+    gemvtc::Plan pl;
+    if (!gemvtc::plan_for(w, m, pl)) return fail(QMM_ERR_UNSUPPORTED, "gemv (mma): layout does not fit shared memory");
+    if (m <= 8)
+        return pl.tpw == 2 ? gemvtc::launch_t<1, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<1, 1, 16>(w, x, m, ep, y, st);
+    return pl.tpw == 2 ? gemvtc::launch_t<2, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<2, 1, 16>(w, x, m, ep, y, st);
 }
 
 }  // namespace qmm
