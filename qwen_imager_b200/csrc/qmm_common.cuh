@@ -99,6 +99,32 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
     return ok != 0;
 }
 
+// Non-blocking probe of a phase (cheaper than try_wait when the phase is
+// already complete, the common case on a well-fed pipeline).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `bar` with parity `parity` to complete.  Returns
 // false (and records `code` in *err unless another error is already there)
 // when the wait exceeds kWaitLimitNs or when another role already failed.
@@ -109,6 +135,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     auto try_once = [&]() {
         return CLUSTER ? mbar_try_wait_cluster(addr, parity) : mbar_try_wait(addr, parity);
     };
+    if (CLUSTER ? mbar_test_wait_cluster(addr, parity) : mbar_test_wait(addr, parity)) return true;
     if (try_once()) return true;
     const uint64_t t0 = global_timer_ns();
     for (;;) {

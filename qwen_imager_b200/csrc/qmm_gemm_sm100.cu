@@ -264,10 +264,10 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         }
     } else if (warp == W::kMma) {
         // ---------------------------------------------------------- MMA issuer
-        if (lane == 0 && leader) {
-            // Kept to a handful of instructions per block: this thread shares its
-            // SM sub-partition with dequantization warps, and every cycle it
-            // waits for an issue slot delays the tensor pipe.
+        // The whole warp runs the loop (warp-uniform control flow keeps the
+        // descriptors and TMEM addresses in uniform registers); one elected
+        // lane issues the MMAs and commits.
+        if (leader) {
             bool ok = true;
             bool issued = false;
             constexpr uint16_t kBoth = 0x3;
@@ -278,36 +278,43 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             int lt = 0;
             for (int tile = unit; ok && tile < p.num_tiles; tile += nunits, ++lt) {
                 const int b = lt & 1;
-                if (!mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma)) {
-                    ok = false;
-                    break;
-                }
+                ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma));
+                if (!ok) break;
                 tc_fence_after_sync();
                 const uint32_t d = tmem + C::kAcc0 + b * T;
                 uint32_t acc = 0;
                 for (int kb = 0; kb < nkb; ++kb) {
-                    if (!mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma) ||
-                        !mbar_wait<PAIR>(PAIR ? &xfull[s] : &full[s], ph_s, p.err, kErrTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
+                    // 1-CTA: afull[a] implies full[s].  The dequantization warps
+                    // that arrive on afull[a] first waited on full[s], the
+                    // barrier the TMA copies of this stage (x tile and codes)
+                    // complete, so the release/acquire chain through afull[a]
+                    // orders the MMA's shared-memory reads after those copies.
+                    // A CTA pair also needs the peer's x tile: xfull[s].
+                    ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma) &&
+                                                     (!PAIR || mbar_wait<PAIR>(&xfull[s], ph_s, p.err,
+                                                                               kErrTimeoutMma)));
+                    if (!ok) break;
                     tc_fence_after_sync();
                     const uint32_t atm = tmem + C::kASlot0 + a * 32;
                     const uint64_t bdesc = bdesc0 + (uint64_t)s * kBStep;
+                    if (lane_elect()) {
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        if constexpr (PAIR) tc_mma_ts_pair(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
-                        else tc_mma_ts(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
-                        acc = 1;
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            if constexpr (PAIR) tc_mma_ts_pair(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
+                            else tc_mma_ts(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
+                            acc = 1;
+                        }
+                        if constexpr (PAIR) {
+                            tc_commit_pair_multicast(&aempty[a], kBoth);
+                            tc_commit_pair_multicast(&sempty[s], kBoth);
+                        } else {
+                            tc_commit(&aempty[a]);
+                            tc_commit(&sempty[s]);
+                        }
                     }
+                    __syncwarp();
+                    acc = 1;
                     issued = true;
-                    if constexpr (PAIR) {
-                        tc_commit_pair_multicast(&aempty[a], kBoth);
-                        tc_commit_pair_multicast(&sempty[s], kBoth);
-                    } else {
-                        tc_commit(&aempty[a]);
-                        tc_commit(&sempty[s]);
-                    }
                     if (++s == S) {
                         s = 0;
                         ph_s ^= 1;
@@ -318,16 +325,21 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     }
                 }
                 if (!ok) break;
-                if constexpr (PAIR) tc_commit_pair_multicast(&acc_full[b], kBoth);
-                else tc_commit(&acc_full[b]);
+                if (lane_elect()) {
+                    if constexpr (PAIR) tc_commit_pair_multicast(&acc_full[b], kBoth);
+                    else tc_commit(&acc_full[b]);
+                }
+                __syncwarp();
             }
             if (!ok && issued) {
-                if constexpr (PAIR) tc_commit_pair_multicast(drain, 0x1);
-                else tc_commit(drain);
+                if (lane_elect()) {
+                    if constexpr (PAIR) tc_commit_pair_multicast(drain, 0x1);
+                    else tc_commit(drain);
+                }
+                __syncwarp();
                 mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain);
             }
         }
-        __syncwarp();
     } else if (warp >= W::kDq0) {
         // ---------------------------------------------------------- dequant
         const int quad = warp & 3;                          // TMEM lane quadrant
@@ -377,21 +389,19 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             }
             uint32_t n0m = 0, n1m = 0;
             if (i + SETS < total_blocks) load_meta(nkb_i, n0m, n1m);
-            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant) ||
-                !mbar_wait<PAIR>(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant))
-                break;
+            // The codes are dequantized as soon as they land; only the store
+            // into the TMEM A slot waits for the MMA that last read the slot.
+            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant)) break;
             const uint8_t *pst = smem + C::kPOff + s * C::kPStageBytes;
-            if constexpr (HALVES == 1) {
-                uint32_t v[32];
-                dequant_row_block<BITS, 0, 2>(pst, m0, m1, row, v, 0);
-                tmem_st_32x32b_x32(tcol + a * 32, v);
-            } else {
-                uint32_t v[16];
-                dequant_row_block<BITS, -1, 1>(pst, m0, m0, row, v, half);
-                tmem_st_32x32b_x16(tcol + a * 32, v);
-            }
+            constexpr int kV = HALVES == 1 ? 32 : 16;
+            uint32_t v[kV];
+            if constexpr (HALVES == 1) dequant_row_block<BITS, 0, 2>(pst, m0, m1, row, v, 0);
+            else dequant_row_block<BITS, -1, 1>(pst, m0, m0, row, v, half);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
+            if (!mbar_wait<PAIR>(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant)) break;
+            if constexpr (HALVES == 1) tmem_st_32x32b_x32(tcol + a * 32, v);
+            else tmem_st_32x32b_x16(tcol + a * 32, v);
             tc_wait_st();
             tc_fence_before_sync();
             __syncwarp();
