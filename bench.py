@@ -80,13 +80,14 @@ def step_flops(layers):
 
 
 def measured_peaks():
+    """(bf16 burst TFLOP/s, bf16 sustained TFLOP/s, HBM GB/s, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d["bf16_tflops"], d["hbm_gbs"], "measured"
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), d["hbm_gbs"], "measured"
     except Exception:
-        return 1590.0, 6650.0, "fallback"
+        return 1590.0, 1400.0, 6650.0, "fallback"
 
 
 def profile_traffic(workload):
@@ -111,6 +112,7 @@ class ClockSampler:
 
     def __init__(self, index):
         self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.power_w, self.limit_w = [], None
         self._stop = threading.Event()
         self._thread = None
         try:
@@ -119,6 +121,10 @@ class ClockSampler:
             self.nv = pynvml
             self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            try:
+                self.limit_w = pynvml.nvmlDeviceGetEnforcedPowerLimit(self.h) / 1000.0
+            except Exception:
+                self.limit_w = None
         except Exception:
             self.nv = None
 
@@ -129,6 +135,10 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    self.power_w.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
+                except Exception:
+                    pass
                 mask = get_reasons(self.h)
                 for bit, name in self.REASONS.items():
                     if mask & bit and bit != 0x1:
@@ -151,8 +161,15 @@ class ClockSampler:
     def summary(self):
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        if self.power_w:
+            # Power draw against the enforced limit shows power capping even
+            # when the sampled reason mask misses it.
+            out["power_w_max"] = round(max(self.power_w), 1)
+            out["power_w_median"] = round(statistics.median(self.power_w), 1)
+            out["power_limit_w"] = self.limit_w
+        return out
 
 
 # --------------------------------------------------------------------- our arm
@@ -307,7 +324,11 @@ def run_ours(args, rank, world, device):
     # Roofline of the dominant kernel (largest FLOP count).
     dom = max(range(len(layers)), key=lambda li: 2.0 * layers[li][0] * layers[li][1] * layers[li][2])
     m, k, n, bits, _ = layers[dom]
-    peak_tf, hbm_gbs, peak_kind = measured_peaks()
+    burst_tf, sustained_tf, hbm_gbs, peak_kind = measured_peaks()
+    # The GEMM is timed inside a loop of back-to-back launches (a long step at
+    # the 1 kW power cap): its denominator is the sustained bf16 figure; the
+    # fraction of the burst figure is reported beside it.
+    peak_tf = sustained_tf
     if m <= 16:
         alg_bytes = n * k * bits / 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
         achieved = alg_bytes / (kernel_ms[dom] * 1e-3) / 1e9
@@ -316,8 +337,12 @@ def run_ours(args, rank, world, device):
     else:
         achieved = 2.0 * m * n * k / (kernel_ms[dom] * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                "frac": round(achieved / peak_tf, 4)}
-    roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback"
+                "frac": round(achieved / peak_tf, 4), "frac_of_burst": round(achieved / burst_tf, 4)}
+    if m <= 16:
+        roof["peak_source"] = f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"
+    else:
+        roof["peak_source"] = (f"{peak_kind} sustained cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops_sustained); "
+                               f"burst {burst_tf}")
     roof["traffic"] = profile_traffic(args.workload)
     roof["kernel_ms"] = round(kernel_ms[dom], 5)
     per_layer = []
@@ -397,12 +422,12 @@ def run_stack(args, rank, world, device):
     lin_flops = cfg.blocks * cfg.linear_flops_per_block()
     att_flops = cfg.blocks * cfg.attention_flops_per_block()
     lin_ms = parts.get("linear", float("nan"))
-    peak_tf, _hbm, peak_kind = measured_peaks()
+    burst_tf, peak_tf, _hbm, peak_kind = measured_peaks()
     achieved = lin_flops / world / (lin_ms * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
-            "frac": round(achieved / peak_tf, 4), "traffic": None,
+            "frac": round(achieved / peak_tf, 4), "frac_of_burst": round(achieved / burst_tf, 4), "traffic": None,
             "kernel": "all quantized linears of one step on rank 0 (GEMMs + modulation GEMVs)",
-            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback"}
+            "peak_source": f"{peak_kind} sustained cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops_sustained)"}
 
     e2e = None
     if not args.no_e2e:
