@@ -146,6 +146,31 @@ QMM_API qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t
                          void *stream);
 
 /*
+ * Split-K factor worth using for a GEMM of m tokens with this weight (1 = none):
+ * > 1 only when the output tiles fill less than half of the SMs (the DiT text
+ * stream, tensor-parallel shards).  Host-only.  No counterpart in quant.rs
+ * (the Metal qmm kernel has one fixed 128x64 tiling, quant.rs:486-489).
+ */
+QMM_API int32_t qmm_gemm_splits(const qmm_weight *w, int64_t m);
+
+/* Bytes of f32 workspace qmm_linear_splitk needs: splits * m * n * 4 (0 for splits <= 1). */
+QMM_API uint64_t qmm_splitk_workspace_bytes(const qmm_weight *w, int64_t m, int32_t splits);
+
+/*
+ * qmm_linear on the tcgen05 GEMM with K split `splits` ways (k / 64 divisible
+ * by splits, n % 4 == 0 when splits > 1): each split writes f32 partial tiles
+ * into `workspace` (caller-owned, 16-byte aligned, qmm_splitk_workspace_bytes
+ * long, not overlapping x or y; no zero-initialisation needed), and a second
+ * kernel sums them and applies the epilogue with one bf16 rounding.  Same
+ * result contract as qmm_linear.  Calls sharing a workspace must be ordered
+ * (one stream).  Replaces, for small-m shapes, the same CustomOp2 "mlx-qmm"
+ * (quant.rs:411-503).
+ */
+QMM_API qmm_status qmm_linear_splitk(const qmm_weight *w, const uint16_t *x, int64_t m,
+                             const qmm_epilogue *ep, uint16_t *y, int32_t splits,
+                             void *workspace, uint64_t workspace_bytes, void *stream);
+
+/*
  * Reads and clears the device-side error word that bounded waits inside the
  * kernels set when they expire (0 = none).  Synchronizes `stream`.  No
  * counterpart in quant.rs (Metal has no bounded waits to report).

@@ -55,6 +55,9 @@ EXPORTED_SYMBOLS = (
     "qmm_linear_ex",
     "qmm_device_error",
     "qmm_launch_count",
+    "qmm_gemm_splits",
+    "qmm_splitk_workspace_bytes",
+    "qmm_linear_splitk",
 )
 
 
@@ -130,6 +133,12 @@ def load() -> ctypes.CDLL:
         lib.qmm_linear.argtypes = [wp, vp, i64, ep, vp, vp]
         lib.qmm_linear_ex.restype = i32
         lib.qmm_linear_ex.argtypes = [wp, vp, i64, ep, vp, i32, vp]
+        lib.qmm_gemm_splits.restype = i32
+        lib.qmm_gemm_splits.argtypes = [wp, i64]
+        lib.qmm_splitk_workspace_bytes.restype = ctypes.c_uint64
+        lib.qmm_splitk_workspace_bytes.argtypes = [wp, i64, i32]
+        lib.qmm_linear_splitk.restype = i32
+        lib.qmm_linear_splitk.argtypes = [wp, vp, i64, ep, vp, i32, vp, ctypes.c_uint64, vp]
         lib.qmm_device_error.restype = i32
         lib.qmm_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
         _lib = lib

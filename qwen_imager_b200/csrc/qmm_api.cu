@@ -187,7 +187,60 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
                     "gemm: %d-bit, group %d, k=%lld is outside the kernel's layouts (needs 4/8-bit, "
                     "k %% 64 == 0, group 32 or a multiple of 64)",
                     w->bits, w->group, (long long)w->k);
-    return qmm::launch_gemm(*w, x, m, e, y, path == QMM_PATH_GEMM_PAIR, st);
+    return qmm::launch_gemm(*w, x, m, e, y, path == QMM_PATH_GEMM_PAIR, 1, nullptr, st);
+}
+
+int32_t qmm_gemm_splits(const qmm_weight *w, int64_t m) {
+    if (!w || qmm_validate(w) != QMM_OK) return 1;
+    return qmm::gemm_recommended_splits(*w, m);
+}
+
+uint64_t qmm_splitk_workspace_bytes(const qmm_weight *w, int64_t m, int32_t splits) {
+    if (!w || m <= 0 || splits <= 1 || w->n <= 0) return 0;
+    return (uint64_t)splits * (uint64_t)m * (uint64_t)w->n * 4u;
+}
+
+qmm_status qmm_linear_splitk(const qmm_weight *w, const uint16_t *x, int64_t m, const qmm_epilogue *ep,
+                             uint16_t *y, int32_t splits, void *workspace, uint64_t workspace_bytes,
+                             void *stream) {
+    qmm_status s = qmm_validate(w);
+    if (s != QMM_OK) return s;
+    if (m < 0) return fail(QMM_ERR_BAD_SHAPE, "negative token count %lld", (long long)m);
+    if (m == 0) return QMM_OK;
+    if (!x || !y) return fail(QMM_ERR_INVALID_ARGUMENT, "null x or y");
+    if (splits < 1 || splits > 16) return fail(QMM_ERR_INVALID_ARGUMENT, "split count %d is not in [1, 16]", splits);
+    qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
+    if (e.activation < QMM_ACT_NONE || e.activation > QMM_ACT_SILU)
+        return fail(QMM_ERR_INVALID_ARGUMENT, "unknown activation %d", e.activation);
+    if (!aligned16(x) || !aligned16(y) || (e.residual && !aligned16(e.residual)))
+        return fail(QMM_ERR_MISALIGNED, "x, y and residual must be 16-byte aligned");
+    {
+        const uintptr_t xb = reinterpret_cast<uintptr_t>(x), yb = reinterpret_cast<uintptr_t>(y);
+        const uintptr_t xe = xb + (uintptr_t)(m * w->k * 2), ye = yb + (uintptr_t)(m * w->n * 2);
+        if (xb < ye && yb < xe) return fail(QMM_ERR_INVALID_ARGUMENT, "y overlaps x");
+    }
+    if (!qmm::gemm_supported(*w))
+        return fail(QMM_ERR_UNSUPPORTED, "gemm: %d-bit, group %d, k=%lld is outside the kernel's layouts",
+                    w->bits, w->group, (long long)w->k);
+    if (splits > 1) {
+        if ((w->k / 64) % splits != 0)
+            return fail(QMM_ERR_INVALID_ARGUMENT, "%d splits do not divide %lld k-blocks of 64", splits,
+                        (long long)(w->k / 64));
+        if (w->n % 4 != 0) return fail(QMM_ERR_UNSUPPORTED, "split-k needs n %% 4 == 0 (n = %lld)", (long long)w->n);
+        const uint64_t need = qmm_splitk_workspace_bytes(w, m, splits);
+        if (!workspace || workspace_bytes < need)
+            return fail(QMM_ERR_INVALID_ARGUMENT, "split-k workspace of %llu bytes is smaller than %llu",
+                        (unsigned long long)workspace_bytes, (unsigned long long)need);
+        if (!aligned16(workspace)) return fail(QMM_ERR_MISALIGNED, "split-k workspace is not 16-byte aligned");
+        const uintptr_t wb = reinterpret_cast<uintptr_t>(workspace), we = wb + (uintptr_t)need;
+        const uintptr_t yb = reinterpret_cast<uintptr_t>(y), ye = yb + (uintptr_t)(m * w->n * 2);
+        const uintptr_t xb = reinterpret_cast<uintptr_t>(x), xe = xb + (uintptr_t)(m * w->k * 2);
+        if ((wb < ye && yb < we) || (wb < xe && xb < we))
+            return fail(QMM_ERR_INVALID_ARGUMENT, "split-k workspace overlaps x or y");
+    }
+    if ((s = check_device()) != QMM_OK) return s;
+    return qmm::launch_gemm(*w, x, m, e, y, false, splits, static_cast<float *>(workspace),
+                            static_cast<cudaStream_t>(stream));
 }
 
 qmm_status qmm_linear(const qmm_weight *w, const uint16_t *x, int64_t m, const qmm_epilogue *ep,

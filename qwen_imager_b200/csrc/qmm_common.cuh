@@ -137,13 +137,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     };
     if (CLUSTER ? mbar_test_wait_cluster(addr, parity) : mbar_test_wait(addr, parity)) return true;
     if (try_once()) return true;
+    // Slow path: back off between probes (32 -> 128 ns) and look at the error
+    // word and the clock only every 16 probes, so that waiting warps leave the
+    // issue slots and the load/store pipe to the warps doing work (a busy
+    // spin of 16 dequantization warps starved the epilogue's stores).
     const uint64_t t0 = global_timer_ns();
-    for (;;) {
+    uint32_t ns = 32;
+    for (uint32_t it = 1;; ++it) {
         if (try_once()) return true;
-        if (*reinterpret_cast<volatile uint32_t *>(err) != kErrNone) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
-            atomicCAS(err, kErrNone, code);
-            return false;
+        __nanosleep(ns);
+        if (ns < 128) ns <<= 1;
+        if ((it & 15) == 0) {
+            if (*reinterpret_cast<volatile uint32_t *>(err) != kErrNone) return false;
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicCAS(err, kErrNone, code);
+                return false;
+            }
         }
     }
 }
@@ -212,6 +221,51 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
 // Named barrier over `threads` threads (id 1..15; id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Tiled TMA stores shared -> global (completion tracked per thread in bulk
+// groups).  The inner coordinate times the element size must be a multiple of
+// 16 bytes and no coordinate may be negative; boxes are clipped at the
+// tensor's bounds.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t c_inner,
+                                             int32_t c_outer) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c_inner), "r"(c_outer)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int32_t c0, int32_t c1,
+                                             int32_t c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's bulk groups beyond the newest N have finished reading shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// This thread's bulk groups have completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier that also returns whether `pred` held in any participating thread.
+__device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t threads, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.or.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(out)
+        : "r"(id), "r"(threads), "r"((uint32_t)pred)
+        : "memory");
+    return out != 0;
 }
 
 // 2-D tiled load issued by either CTA of a CTA pair: data lands in this CTA's

@@ -14,7 +14,8 @@
 // TMEM so that the epilogue of one tile overlaps the main loop of the next.
 //
 // Warp roles (one persistent CTA per SM):
-//   warps 0-3        epilogue: TMEM -> registers, bias/act/gate/residual, bf16 stores
+//   warps 0-3        epilogue: TMEM -> registers, bias/act/gate/residual in f32,
+//                    bf16 chunks staged in shared memory and written by TMA stores
 //   next 4*SETS      dequant: packed codes (smem) -> bf16 -> TMEM A slots; SETS
 //                    groups of four warps take alternate K-blocks so several
 //                    blocks are in flight
@@ -68,11 +69,15 @@ struct Cfg {
     static constexpr int kStageBytes = kXStageBytes + kPStageBytes;
     // TMEM: two T-column accumulators, the rest as 32-column A slots (at most 8).
     static constexpr int kASlots = (512 - 2 * T) / 32 > 8 ? 8 : (512 - 2 * T) / 32;
-    static constexpr int kSmemBudget = 227 * 1024 - 2048;
+    // Epilogue staging: one 32-token chunk of the 128-row tile, [32][128] f32
+    // (bf16 outputs use the first half), written back with 16-byte stores.
+    static constexpr int kEStageBytes = 32 * kWRows * 4;
+    static constexpr int kSmemBudget = 227 * 1024 - 2048 - kEStageBytes;
     static constexpr int kStages = kSmemBudget / kStageBytes > 8 ? 8 : kSmemBudget / kStageBytes;
     static constexpr int kXOff = 0;
     static constexpr int kPOff = kXOff + kStages * kXStageBytes;
-    static constexpr int kBarOff = kPOff + kStages * kPStageBytes;
+    static constexpr int kEOff = kPOff + kStages * kPStageBytes;
+    static constexpr int kBarOff = kEOff + kEStageBytes;
     static constexpr int kNumBars = 3 * kStages + 2 * 8 + 4 + 1;
     static constexpr int kTmemPtrOff = kBarOff + kNumBars * 8;
     static constexpr int kSmemBytes = kTmemPtrOff + 16 + 1024;  // + alignment slack
@@ -85,14 +90,19 @@ struct Cfg {
     static constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * kWRows : kWRows, T);
 };
 
+// Work unit u of num_units = tiles * splits covers output tile u % tiles and
+// k-blocks [split * kbs, (split + 1) * kbs) with split = u / tiles.  With
+// splits > 1 the epilogue writes f32 partial tiles to ws[split][m][n] and
+// qmm_splitk_reduce_kernel applies the epilogue.
 struct Params {
     const uint16_t *scales;
     const uint16_t *offsets;
     uint16_t *y;
+    float *ws;
     EpilogueArgs ep;
     int32_t m, n, k;
     int32_t group, groups, group_shift;
-    int32_t w_tiles, num_tiles;
+    int32_t w_tiles, tiles, num_units, splits, kbs;
     uint32_t *err;
 };
 
@@ -149,7 +159,8 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
 template <int BITS, int T, int SETS, int HALVES, bool PAIR>
 __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                    const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_w,
+                    const __grid_constant__ CUtensorMap tmap_out, const Params p) {
     using C = Cfg<BITS, T, PAIR>;
     using W = Warps<SETS, HALVES>;
     constexpr int S = C::kStages;
@@ -206,14 +217,15 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     if (warp == W::kProducer && lane == 0) {
         tma_prefetch_desc(&tmap_x);
         tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_out);
     }
     tc_fence_before_sync();
     __syncthreads();
     if constexpr (PAIR) cluster_sync();  // peer barriers initialized, TMEM allocated in both CTAs
     tc_fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    const int nkb = p.k / kBK;
-    const int local_tiles = (p.num_tiles - unit + nunits - 1) / nunits;
+    const int nkb = p.kbs;  // k-blocks per work unit
+    const int local_tiles = (p.num_units - unit + nunits - 1) / nunits;
     const uint32_t total_blocks = (uint32_t)local_tiles * (uint32_t)nkb;
     // Barriers of the pair's leader that every CTA of the pair signals.
     auto leader_bar = [&](uint64_t *bar) { return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar); };
@@ -228,10 +240,11 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         bool ok = true;
         int s = 0;
         uint32_t ph_s = 0;
-        for (int tile = unit; ok && tile < p.num_tiles; tile += nunits) {
+        for (int wu = unit; ok && wu < p.num_units; wu += nunits) {
+            const int tile = wu % p.tiles, kb0 = (wu / p.tiles) * nkb;
             const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
             const int m0 = (tile / p.w_tiles) * T + (int)rank * C::kXRows;
-            for (int kb = 0; kb < nkb; ++kb, ++i) {
+            for (int kb = kb0; kb < kb0 + nkb; ++kb, ++i) {
                 if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer)) {
                     ok = false;
                     break;
@@ -276,7 +289,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             int s = 0, a = 0;
             uint32_t ph_s = 0, ph_a = 0;
             int lt = 0;
-            for (int tile = unit; ok && tile < p.num_tiles; tile += nunits, ++lt) {
+            for (int wu = unit; ok && wu < p.num_units; wu += nunits, ++lt) {
                 const int b = lt & 1;
                 ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma));
                 if (!ok) break;
@@ -349,22 +362,27 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         const int row = quad * 32 + lane;                   // weight row within the tile
         const uint32_t tcol = tmem + (static_cast<uint32_t>(quad * 32) << 16) + C::kASlot0 + half * 16;
         const int gshift = p.group_shift;
-        // This thread's scale/offset row pointers for a tile (null past n).
+        // This thread's scale/offset row pointers for a work unit (null past
+        // n), offset to the unit's first k-block.
         const uint16_t *sp = nullptr, *op = nullptr;
+        int kbase = 0;
         auto set_tile = [&](int tile_local) {
-            const int tile = unit + tile_local * nunits;
+            const int wu = unit + tile_local * nunits;
+            const int tile = wu % p.tiles;
             const int n = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows + row;
+            kbase = (wu / p.tiles) * nkb;
             sp = op = nullptr;
-            if (tile < p.num_tiles && n < p.n) {
+            if (wu < p.num_units && n < p.n) {
                 sp = p.scales + (int64_t)n * p.groups;
                 op = p.offsets + (int64_t)n * p.groups;
             }
         };
-        // (scale | offset << 16) of the group(s) this warp needs in block kb.
+        // (scale | offset << 16) of the group(s) this warp needs in block kb
+        // of the current work unit.
         auto load_meta = [&](int kb, uint32_t &m0, uint32_t &m1) {
             m0 = m1 = 0;
             if (sp) {
-                const int c0 = kb * kBK + (HALVES == 2 ? half * 32 : 0);
+                const int c0 = (kbase + kb) * kBK + (HALVES == 2 ? half * 32 : 0);
                 const int g0 = c0 >> gshift;
                 const int g1 = (c0 + 32) >> gshift;
                 m0 = (uint32_t)__ldg(sp + g0) | ((uint32_t)__ldg(op + g0) << 16);
@@ -425,12 +443,17 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         const int quad = warp;
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int lt = 0;
-        for (int tile = unit; tile < p.num_tiles; tile += nunits, ++lt) {
+        uint32_t chunk = 0;  // write-back chunks so far (staging buffer parity)
+        for (int wu = unit; wu < p.num_units; wu += nunits, ++lt) {
             const int b = lt & 1;
             const uint32_t u = lt >> 1;
+            const int tile = wu % p.tiles, split = wu / p.tiles;
             const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
             const int m0 = (tile / p.w_tiles) * T;
-            if (!mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue)) break;
+            // The four epilogue warps leave together (they meet at named
+            // barriers below): one expired wait ends the loop for all.
+            const bool waited = mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue);
+            if (named_barrier_or(1, kEpiWarps * 32, !waited)) break;
             tc_fence_after_sync();
             const int64_t n = n0 + quad * 32 + lane;
             const bool nvalid = n < p.n;
@@ -446,32 +469,72 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     __syncwarp();
                     if (lane == 0) arrive_leader(&acc_empty[b]);
                 }
-                if (nvalid) {
-                    // Residual values of 8 tokens are loaded before any of
-                    // their outputs is stored: y may alias the residual, so
-                    // interleaved load/store pairs would serialize on memory
-                    // latency.  Each thread reads only elements it writes.
-                    const int64_t mrow = m0 + c0;
-                    const int lim = (int)(p.m - mrow < 32 ? p.m - mrow : 32);
+                // Write-back of the chunk (32 tokens x 128 rows of the tile):
+                // values go to a shared-memory staging tile that one thread
+                // hands to the copy engine as one TMA store (8 KB bf16, 16 KB
+                // f32; clipped at the m and n edges).  Per-thread global stores
+                // of 64-byte row pieces were limited by outstanding stores per
+                // SM, and per-row bulk copies by copy-engine issue.  bf16
+                // chunks alternate between two staging buffers; f32 (split-K)
+                // chunks use one.  Rows of y that are not 16-byte aligned
+                // (n % 8 != 0) are written with element stores instead.
+                const int64_t mrow = m0 + c0;
+                const int lim = (int)(p.m - mrow < 32 ? p.m - mrow : 32);
+                const int nrow = (int)(p.n - n0 < kWRows ? p.n - n0 : kWRows);  // valid rows of the tile
+                const int eb = p.ws ? 0 : (chunk & 1);
+                uint8_t *stg = smem + C::kEOff + eb * (C::kEStageBytes / 2);
+                // The bulk stores that last read this staging buffer are done reading.
+                if (quad == 0 && lane == 0) {
+                    if (p.ws) bulk_wait_read<0>();
+                    else bulk_wait_read<1>();
+                }
+                named_barrier(1, kEpiWarps * 32);
+                if (p.ws) {
+                    // Split-K: the f32 partial chunk, no epilogue (applied by the reduction).
+                    float *st32 = reinterpret_cast<float *>(smem + C::kEOff);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) st32[j * kWRows + quad * 32 + lane] = __uint_as_float(v[j]);
+                } else {
+                    // Epilogue in f32, one bf16 rounding.  Residual values of 8
+                    // tokens are loaded before the chunk is written back (y
+                    // may alias the residual; this chunk's residual elements
+                    // are all read before its bulk stores are issued).
+                    uint16_t *st16 = reinterpret_cast<uint16_t *>(stg);
 #pragma unroll
                     for (int h = 0; h < 32; h += 8) {
                         float rv[8];
                         if (p.ep.residual) {
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
-                                rv[j] = h + j < lim ? bf16_bits_to_f32(p.ep.residual[(mrow + h + j) * p.n + n]) : 0.0f;
+                                rv[j] = (nvalid && h + j < lim) ? bf16_bits_to_f32(p.ep.residual[(mrow + h + j) * p.n + n])
+                                                                : 0.0f;
                         }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            if (h + j < lim) {
-                                const float val = epilogue_value_rv(p.ep, fc, __uint_as_float(v[h + j]), rv[j]);
-                                p.y[(mrow + h + j) * p.n + n] = f32_to_bf16_bits(val);
-                            }
-                        }
+                        for (int j = 0; j < 8; ++j)
+                            st16[(h + j) * kWRows + quad * 32 + lane] =
+                                f32_to_bf16_bits(epilogue_value_rv(p.ep, fc, __uint_as_float(v[h + j]), rv[j]));
                     }
                 }
+                fence_proxy_async_smem();
+                named_barrier(1, kEpiWarps * 32);
+                if (!p.ws && (p.n & 7) != 0) {
+                    // Rows of y not 16-byte aligned (n % 8 != 0): element stores
+                    // by all epilogue threads; the next chunk's first barrier
+                    // orders these reads before the buffer is rewritten.
+                    const uint16_t *st16 = reinterpret_cast<const uint16_t *>(stg);
+                    for (int q = quad * 32 + lane; q < 32 * kWRows; q += kEpiWarps * 32) {
+                        const int row = q / kWRows, col = q % kWRows;
+                        if (row < lim && col < nrow) p.y[(mrow + row) * p.n + n0 + col] = st16[row * kWRows + col];
+                    }
+                } else if (quad == 0 && lane == 0 && lim > 0 && nrow > 0) {
+                    if (p.ws) tma_store_3d(&tmap_out, smem + C::kEOff, n0, (int32_t)mrow, split);
+                    else tma_store_2d(&tmap_out, stg, n0, (int32_t)mrow);
+                }
+                if (quad == 0 && lane == 0) bulk_commit();
+                ++chunk;
             }
         }
+        if (quad == 0 && lane == 0) bulk_wait_all();  // the stores have landed before the CTA exits
     }
 
     // ------------------------------------------------------------------ teardown
@@ -483,6 +546,36 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         tc_fence_after_sync();
         if constexpr (PAIR) tmem_dealloc_pair(tmem, kTmemCols);
         else tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Split-K reduction: y = epilogue(sum over splits of ws[split]), f32, one
+// bf16 rounding; 4 consecutive outputs of a row per thread.
+__global__ void __launch_bounds__(256) qmm_splitk_reduce_kernel(const float *__restrict__ ws, int splits,
+                                                                int64_t m, int64_t n, EpilogueArgs ep,
+                                                                uint16_t *y) {
+    const int64_t quads = m * (n / 4);
+    const int64_t plane = m * n;
+    for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < quads;
+         q += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = q / (n / 4), col = (q - row * (n / 4)) * 4;
+        const int64_t idx = row * n + col;
+        float4 acc = *reinterpret_cast<const float4 *>(ws + idx);
+        for (int sp = 1; sp < splits; ++sp) {
+            const float4 v = *reinterpret_cast<const float4 *>(ws + sp * plane + idx);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+        uint16_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const FeatureConsts fc = load_feature_consts(ep, col + j, true);
+            o[j] = f32_to_bf16_bits(epilogue_value(ep, fc, a[j], ep.residual ? ep.residual + idx + j : nullptr));
+        }
+        *reinterpret_cast<uint2 *>(y + idx) = make_uint2(o[0] | ((uint32_t)o[1] << 16), o[2] | ((uint32_t)o[3] << 16));
     }
 }
 
@@ -524,9 +617,24 @@ static qmm_status make_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, int e
     return QMM_OK;
 }
 
+static qmm_status make_map_3d_f32(CUtensorMap *map, const void *base, uint64_t inner, uint64_t mid,
+                                  uint64_t outer, uint32_t box_inner, uint32_t box_mid) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(QMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {inner, mid, outer};
+    cuuint64_t strides[2] = {inner * 4, inner * mid * 4};
+    cuuint32_t box[3] = {box_inner, box_mid, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(QMM_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return QMM_OK;
+}
+
 template <int BITS, int T, int SETS, int HALVES, bool PAIR>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
-                           const qmm_epilogue &ep, uint16_t *y, cudaStream_t st) {
+                           const qmm_epilogue &ep, uint16_t *y, int splits, float *ws, cudaStream_t st) {
     using C = Cfg<BITS, T, PAIR>;
     auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR>;
     static bool configured[64] = {};
@@ -549,11 +657,26 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
                     words * 4, C::kPWords, kWRows,
                     BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (s != QMM_OK) return s;
+    // Output map for the epilogue's TMA stores: y [m, n] bf16, or for split-K
+    // the workspace [splits, m, n] f32; box 128 rows of the tile x 32 tokens.
+    // y rows that are not 16-byte aligned (n % 8 != 0) use element stores and
+    // get a placeholder map.
+    CUtensorMap tout;
+    if (splits > 1) {
+        s = make_map_3d_f32(&tout, ws, (uint64_t)w.n, (uint64_t)m, (uint64_t)splits, kWRows, 32);
+    } else if (w.n % 8 == 0) {
+        s = make_map_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, (uint64_t)w.n, (uint64_t)m,
+                        (uint64_t)w.n * 2, kWRows, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        tout = tw;
+    }
+    if (s != QMM_OK) return s;
 
     Params p;
     p.scales = w.scales;
     p.offsets = w.biases;
     p.y = y;
+    p.ws = splits > 1 ? ws : nullptr;
     p.ep = EpilogueArgs{ep.bias, ep.gate, ep.residual, ep.activation};
     p.m = (int32_t)m;
     p.n = (int32_t)w.n;
@@ -565,10 +688,13 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     constexpr int kTileRows = PAIR ? 2 * kWRows : kWRows;
     p.w_tiles = (int32_t)((w.n + kTileRows - 1) / kTileRows);
     const int64_t t_tiles = (m + T - 1) / T;
-    p.num_tiles = (int32_t)(p.w_tiles * t_tiles);
+    p.tiles = (int32_t)(p.w_tiles * t_tiles);
+    p.splits = splits;
+    p.kbs = (int32_t)(w.k / kBK / splits);
+    p.num_units = p.tiles * splits;
     p.err = device_error_word();
     const int ctas = PAIR ? 2 : 1;
-    const int units = (int)std::min<int64_t>(p.num_tiles, sm_count() / ctas);
+    const int units = (int)std::min<int64_t>(p.num_units, sm_count() / ctas);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.gridDim = dim3(units * ctas, 1, 1);
@@ -581,10 +707,19 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, tout, p);
     count_launch();
     if (e == cudaSuccess) e = cudaGetLastError();
-    return e == cudaSuccess ? QMM_OK : cuda_fail(e, "gemm launch");
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+    if (splits > 1) {
+        const int64_t quads = m * (w.n / 4);
+        const int blocks = (int)std::min<int64_t>((quads + 255) / 256, (int64_t)sm_count() * 8);
+        qmm_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(ws, splits, m, w.n, p.ep, y);
+        count_launch();
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "split-k reduce launch");
+    }
+    return QMM_OK;
 }
 
 }  // namespace gemm
@@ -598,19 +733,37 @@ bool gemm_supported(const qmm_weight &w) {
     return true;
 }
 
+int gemm_recommended_splits(const qmm_weight &w, int64_t m) {
+    // Split K only when the output tiles fill less than half of the SMs
+    // (e.g. the DiT text stream, m = 256..512, or tensor-parallel shards):
+    // the largest divisor of the k-block count, up to 8, that keeps the work
+    // units within one wave.
+    if (m <= 0 || w.n % 4 != 0 || !gemm_supported(w)) return 1;
+    const int64_t tiles = ((w.n + gemm::kWRows - 1) / gemm::kWRows) * ((m + 191) / 192);
+    const int sms = sm_count();
+    if (tiles * 2 > sms) return 1;
+    const int64_t nkb = w.k / gemm::kBK;
+    int best = 1;
+    // At least 8 k-blocks per split: below that the second (reduction) kernel
+    // costs more than the idle SMs (measured at k = 384).
+    for (int sp = 2; sp <= 8; ++sp)
+        if (nkb % sp == 0 && nkb / sp >= 8 && tiles * sp <= sms) best = sp;
+    return best;
+}
+
 qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
-                       uint16_t *y, bool pair, cudaStream_t st) {
+                       uint16_t *y, bool pair, int splits, float *ws, cudaStream_t st) {
     if (m > (int64_t)INT32_MAX - 256) return fail(QMM_ERR_UNSUPPORTED, "gemm: m too large");
     // Token tile 192 (two 192-column accumulators + four A slots fill TMEM);
     // four dequantization warp sets of full rows.  CTA pairs (cta_group::2)
     // on request: they halve the x traffic per SM but lengthen the A-slot
     // hand-off by a cross-SM round trip, which measured slower on B200.
-    pair = pair && w.n > gemm::kWRows;
+    pair = pair && w.n > gemm::kWRows && splits == 1;
     if (w.bits == 4)
-        return pair ? gemm::launch_t<4, 192, 4, 1, true>(w, x, m, ep, y, st)
-                    : gemm::launch_t<4, 192, 4, 1, false>(w, x, m, ep, y, st);
-    return pair ? gemm::launch_t<8, 192, 4, 1, true>(w, x, m, ep, y, st)
-                : gemm::launch_t<8, 192, 4, 1, false>(w, x, m, ep, y, st);
+        return pair ? gemm::launch_t<4, 192, 4, 1, true>(w, x, m, ep, y, 1, nullptr, st)
+                    : gemm::launch_t<4, 192, 4, 1, false>(w, x, m, ep, y, splits, ws, st);
+    return pair ? gemm::launch_t<8, 192, 4, 1, true>(w, x, m, ep, y, 1, nullptr, st)
+                : gemm::launch_t<8, 192, 4, 1, false>(w, x, m, ep, y, splits, ws, st);
 }
 
 }  // namespace qmm

@@ -43,6 +43,20 @@ def _stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_workspaces = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Split-K scratch for the current stream of `device`, grown on demand.
+    Kernels on one stream run in order, so one buffer per stream suffices."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
 def _require_cuda(t: torch.Tensor, what: str) -> None:
     if t.device.type != "cuda":
         raise QmmError(_lib.QMM_ERR_CUDA, f"{what} is on {t.device}; the quantized linear runs on CUDA only")
@@ -87,8 +101,14 @@ class Affine:
 
     def run(self, x2d: torch.Tensor, *, gate: Optional[torch.Tensor] = None,
             residual: Optional[torch.Tensor] = None, activation: Optional[str] = None,
-            out: Optional[torch.Tensor] = None, path: int = _lib.QMM_PATH_AUTO) -> torch.Tensor:
-        """y [m, output] = residual + gate * act(x2d . W^T + bias), one launch."""
+            out: Optional[torch.Tensor] = None, path: int = _lib.QMM_PATH_AUTO,
+            splits: Optional[int] = None) -> torch.Tensor:
+        """y [m, output] = residual + gate * act(x2d . W^T + bias).
+
+        The GEMM (m > 16 under QMM_PATH_AUTO, or QMM_PATH_GEMM) splits K when
+        the output tiles alone would leave most SMs idle; `splits` forces a
+        split count (1 = none).  The f32 workspace comes from a per-device,
+        per-stream cache."""
         m = int(x2d.shape[0])
         n = self.output
         if out is None:
@@ -101,8 +121,22 @@ class Affine:
             gate = gate.reshape(n).to(torch.bfloat16).contiguous()
         ep = QmmEpilogue(_ptr(self.bias), _ptr(gate), _ptr(residual), ACTIVATIONS[activation])
         w = self.c_weight()
-        status = _lib.load().qmm_linear_ex(ctypes.byref(w), x2d.data_ptr(), m, ctypes.byref(ep),
-                                           out.data_ptr(), path, _stream_handle(x2d.device))
+        lib = _lib.load()
+        gemm = path == _lib.QMM_PATH_GEMM or (path == _lib.QMM_PATH_AUTO and m > 16)
+        if gemm and m > 0:
+            sp = lib.qmm_gemm_splits(ctypes.byref(w), m) if splits is None else int(splits)
+            if sp > 1:
+                nbytes = int(lib.qmm_splitk_workspace_bytes(ctypes.byref(w), m, sp))
+                ws = _workspace(x2d.device, nbytes)
+                status = lib.qmm_linear_splitk(ctypes.byref(w), x2d.data_ptr(), m, ctypes.byref(ep),
+                                               out.data_ptr(), sp, ws.data_ptr(), nbytes,
+                                               _stream_handle(x2d.device))
+                if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
+                    return self._dense_fallback(x2d, gate, residual, activation, out)
+                _lib.check(status)
+                return out
+        status = lib.qmm_linear_ex(ctypes.byref(w), x2d.data_ptr(), m, ctypes.byref(ep),
+                                   out.data_ptr(), path, _stream_handle(x2d.device))
         if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
             return self._dense_fallback(x2d, gate, residual, activation, out)
         _lib.check(status)
@@ -196,7 +230,7 @@ class Linear:
     def forward_fused(self, x: torch.Tensor, *, gate: Optional[torch.Tensor] = None,
                       residual: Optional[torch.Tensor] = None,
                       activation: Optional[str] = None, path: int = _lib.QMM_PATH_AUTO,
-                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, splits: Optional[int] = None) -> torch.Tensor:
         """residual + gate * act(x . W^T + bias) with any leading dims on x.
 
         gate: [output] per-feature multiplier; residual: same shape as the output.
@@ -229,7 +263,7 @@ class Linear:
             x2d = x2d.contiguous()
         if out is not None:
             out = out.view(m, a.output)
-        y = a.run(x2d, gate=gate, residual=residual, activation=activation, out=out, path=path)
+        y = a.run(x2d, gate=gate, residual=residual, activation=activation, out=out, path=path, splits=splits)
         return y.reshape(*lead, a.output)
 
 

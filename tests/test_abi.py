@@ -87,3 +87,15 @@ def test_compute_entry_points_fail_loudly_without_a_device():
     assert st == _lib.QMM_ERR_CUDA
     st = lib.qmm_dequantize(ctypes.byref(w), 0x8000, 0, None)
     assert st == _lib.QMM_ERR_CUDA
+
+
+def test_splitk_workspace_size_and_argument_checks_without_a_device():
+    from qwen_imager_b200 import _lib
+    lib = _lib.load()
+    import ctypes
+    w = _lib.QmmWeight(16, 16, 16, 96, 640, 4, 64)
+    assert lib.qmm_splitk_workspace_bytes(ctypes.byref(w), 8, 2) == 2 * 8 * 96 * 4
+    assert lib.qmm_splitk_workspace_bytes(ctypes.byref(w), 8, 1) == 0
+    # split count outside [1, 16] and a null workspace are argument errors, found before any device access
+    assert lib.qmm_linear_splitk(ctypes.byref(w), 16, 8, None, 1 << 20, 0, 0, 0, None) == _lib.QMM_ERR_INVALID_ARGUMENT
+    assert lib.qmm_linear_splitk(ctypes.byref(w), 16, 8, None, 1 << 20, 2, 0, 0, None) == _lib.QMM_ERR_INVALID_ARGUMENT
