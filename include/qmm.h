@@ -171,6 +171,24 @@ QMM_API qmm_status qmm_linear_splitk(const qmm_weight *w, const uint16_t *x, int
                              void *workspace, uint64_t workspace_bytes, void *stream);
 
 /*
+ * qmm_linear_splitk with the f32 scratch in a static device array of the
+ * library (qmm_static_scratch_bytes() = 16 MiB per device) instead of a
+ * caller workspace: allocates nothing.  No counterpart in quant.rs.
+ *   - splits * m * n * 4 bytes must fit the scratch; larger requests return
+ *     QMM_ERR_UNSUPPORTED before any launch;
+ *   - nothing in the scratch must start at zero;
+ *   - every call on a device uses the same scratch: calls that may overlap in
+ *     time (other streams, threads) race, so order them on one stream;
+ *   - the first call on a device resolves the scratch address with a runtime
+ *     call; make it before any stream capture.
+ */
+QMM_API qmm_status qmm_linear_splitk_static(const qmm_weight *w, const uint16_t *x, int64_t m,
+                                    const qmm_epilogue *ep, uint16_t *y, int32_t splits, void *stream);
+
+/* Size in bytes of the static scratch behind qmm_linear_splitk_static. */
+QMM_API uint64_t qmm_static_scratch_bytes(void);
+
+/*
  * Reads and clears the device-side error word that bounded waits inside the
  * kernels set when they expire (0 = none).  Synchronizes `stream`.  No
  * counterpart in quant.rs (Metal has no bounded waits to report).

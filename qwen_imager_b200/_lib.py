@@ -58,6 +58,8 @@ EXPORTED_SYMBOLS = (
     "qmm_gemm_splits",
     "qmm_splitk_workspace_bytes",
     "qmm_linear_splitk",
+    "qmm_linear_splitk_static",
+    "qmm_static_scratch_bytes",
 )
 
 
@@ -139,6 +141,10 @@ def load() -> ctypes.CDLL:
         lib.qmm_splitk_workspace_bytes.argtypes = [wp, i64, i32]
         lib.qmm_linear_splitk.restype = i32
         lib.qmm_linear_splitk.argtypes = [wp, vp, i64, ep, vp, i32, vp, ctypes.c_uint64, vp]
+        lib.qmm_linear_splitk_static.restype = i32
+        lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
+        lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64
+        lib.qmm_static_scratch_bytes.argtypes = []
         lib.qmm_device_error.restype = i32
         lib.qmm_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
         _lib = lib

@@ -1,0 +1,75 @@
+// qmm_linear_splitk_static: the split-K GEMM with its f32 partial-sum scratch
+// in a file-scope device array instead of a caller-provided workspace, for
+// callers that cannot allocate device memory.  Nothing is allocated: the
+// scratch is part of the library's device image (one copy per device), and its
+// address is resolved once per device with cudaGetSymbolAddress.
+//
+// Contract (also stated in include/qmm.h):
+//   - at most kStaticScratchBytes (16 MiB) of scratch: splits * m * n * 4 bytes;
+//     larger requests fail with QMM_ERR_UNSUPPORTED before anything is launched;
+//   - nothing in the scratch has to start at zero: every split writes its
+//     whole partial tile before the reduction reads it;
+//   - all calls on a device share the one scratch array, so calls that may
+//     overlap in time (different streams, host threads, processes sharing a
+//     context) race; order them on one stream;
+//   - the first call on a device resolves the scratch address (a runtime
+//     call, not a stream operation): make it before any stream capture.
+#include <mutex>
+
+#include "qmm_internal.h"
+
+namespace qmm {
+namespace {
+
+constexpr uint64_t kStaticScratchBytes = 16ull << 20;
+constexpr int kMaxScratchDevices = 64;
+
+static __device__ __align__(256) float g_static_scratch[kStaticScratchBytes / sizeof(float)];
+
+std::mutex g_scratch_mutex;
+void *g_scratch_addr[kMaxScratchDevices] = {};
+
+qmm_status static_scratch(void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "no CUDA device");
+    if (dev < 0 || dev >= kMaxScratchDevices)
+        return fail(QMM_ERR_UNSUPPORTED, "device %d is beyond the %d devices the static scratch serves", dev,
+                    kMaxScratchDevices);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "static scratch address");
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return QMM_OK;
+}
+
+}  // namespace
+}  // namespace qmm
+
+extern "C" {
+
+uint64_t qmm_static_scratch_bytes(void) { return qmm::kStaticScratchBytes; }
+
+qmm_status qmm_linear_splitk_static(const qmm_weight *w, const uint16_t *x, int64_t m,
+                                    const qmm_epilogue *ep, uint16_t *y, int32_t splits, void *stream) {
+    if (!w) return qmm::fail(QMM_ERR_INVALID_ARGUMENT, "null weight");
+    const uint64_t need = qmm_splitk_workspace_bytes(w, m, splits);
+    if (need > qmm::kStaticScratchBytes)
+        return qmm::fail(QMM_ERR_UNSUPPORTED,
+                         "split-k with %d splits of %lld x %lld needs %llu bytes of scratch; the static scratch "
+                         "holds %llu (use qmm_linear_splitk with a caller workspace, or fewer splits)",
+                         splits, (long long)m, (long long)w->n, (unsigned long long)need,
+                         (unsigned long long)qmm::kStaticScratchBytes);
+    void *scratch = nullptr;
+    if (need > 0) {
+        qmm_status s = qmm::static_scratch(&scratch);
+        if (s != QMM_OK) return s;
+    }
+    return qmm_linear_splitk(w, x, m, ep, y, splits, scratch, qmm::kStaticScratchBytes, stream);
+}
+
+}  // extern "C"

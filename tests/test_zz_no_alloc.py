@@ -1,0 +1,65 @@
+"""The no-allocation split-K entry point (qmm_linear_splitk_static) against the
+caller-workspace one (qmm_linear_splitk): same kernels, same results, on two
+calls in a row; oversize requests are refused.  Kept in its own file, collected
+last, so it runs both alone and after every other test."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from qmm_testutil import from_dev_bf16, make_linear, random_layer, sin_input, to_dev_u16
+from qwen_imager_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _call_workspace(lib, lin, x, m, splits, y):
+    w = lin.affine.c_weight()
+    nbytes = int(lib.qmm_splitk_workspace_bytes(ctypes.byref(w), m, splits))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.qmm_linear_splitk(ctypes.byref(w), x.data_ptr(), m, None, y.data_ptr(), splits, ws.data_ptr(),
+                                     nbytes, st))
+
+
+def _call_static(lib, lin, x, m, splits, y):
+    w = lin.affine.c_weight()
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.qmm_linear_splitk_static(ctypes.byref(w), x.data_ptr(), m, None, y.data_ptr(), splits, st))
+
+
+@pytest.mark.parametrize("m,k,n,bits,splits", [(256, 3072, 3072, 4, 3), (200, 1024, 768, 8, 4)])
+def test_static_scratch_matches_caller_workspace_twice(oracle, m, k, n, bits, splits):
+    lib = _lib.load()
+    packed, scales, offsets, bias = random_layer(n, k, bits, 64, seed=m + n, bias=True)
+    lin = make_linear(packed, scales, offsets, bias, bits, 64)
+    x = to_dev_u16(sin_input(m, k))
+    ref = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    _call_workspace(lib, lin, x, m, splits, ref)
+    torch.cuda.synchronize()
+    want = oracle.bf16_to_f32(from_dev_bf16(ref))
+    for _ in range(2):  # two calls in a row reuse the same scratch
+        y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        _call_static(lib, lin, x, m, splits, y)
+        torch.cuda.synchronize()
+        got = oracle.bf16_to_f32(from_dev_bf16(y))
+        assert np.isfinite(got).all()
+        # same kernels and summation order: within a bf16 rounding of the workspace path
+        assert np.abs(got - want).max() <= np.abs(want).max() * 2.0**-8
+
+
+def test_static_scratch_refuses_oversize_requests():
+    lib = _lib.load()
+    cap = int(lib.qmm_static_scratch_bytes())
+    assert cap == 16 << 20
+    packed, scales, offsets, bias = random_layer(4096, 1024, 4, 64, seed=2, bias=False)
+    lin = make_linear(packed, scales, offsets, bias, 4, 64)
+    m, splits = 4096, 2  # 2 * 4096 * 4096 * 4 bytes = 128 MiB
+    x = torch.zeros((m, 1024), dtype=torch.bfloat16, device="cuda")
+    y = torch.empty((m, 4096), dtype=torch.bfloat16, device="cuda")
+    w = lin.affine.c_weight()
+    status = lib.qmm_linear_splitk_static(ctypes.byref(w), x.data_ptr(), m, None, y.data_ptr(), splits,
+                                          torch.cuda.current_stream().cuda_stream)
+    assert status == _lib.QMM_ERR_UNSUPPORTED
+    assert b"static scratch" in lib.qmm_last_error()
