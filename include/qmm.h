@@ -171,6 +171,18 @@ QMM_API qmm_status qmm_linear_splitk(const qmm_weight *w, const uint16_t *x, int
                              void *workspace, uint64_t workspace_bytes, void *stream);
 
 /*
+ * Fused LayerNorm (no affine, f32 statistics) and adaLN modulation of a DiT
+ * block input: out = bf16((x - mean) / sqrt(var + eps) * (1 + scale) + shift),
+ * x and out bf16 [rows, hidden], shift and scale bf16 [hidden]; hidden a
+ * multiple of 256 up to 4096; 16-byte aligned pointers; out may alias x.
+ * Replaces the separate norm and modulation tensor ops around every DiT linear
+ * input (src/dit.rs:50, 91).
+ */
+QMM_API qmm_status qmm_layernorm_modulate(const uint16_t *x, int64_t rows, int64_t hidden,
+                                  const uint16_t *shift, const uint16_t *scale, float eps,
+                                  uint16_t *out, void *stream);
+
+/*
  * qmm_linear_splitk with the f32 scratch in a static device array of the
  * library (qmm_static_scratch_bytes() = 16 MiB per device) instead of a
  * caller workspace: allocates nothing.  No counterpart in quant.rs.
@@ -194,6 +206,14 @@ QMM_API uint64_t qmm_static_scratch_bytes(void);
  * counterpart in quant.rs (Metal has no bounded waits to report).
  */
 QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
+
+/*
+ * Caps the persistent kernels' grids at `sms` CTAs (0 = every SM) for launches
+ * made after the call, in this process; returns the previous cap.  Leaves SMs
+ * free for kernels that run concurrently on other streams (e.g. a collective
+ * overlapping a row-parallel GEMM).  No counterpart in quant.rs.
+ */
+QMM_API int32_t qmm_set_sm_budget(int32_t sms);
 
 /* Number of kernels this library has launched in the calling process (kernels
  * captured into a CUDA graph count once, at capture).  No counterpart in quant.rs. */

@@ -59,6 +59,8 @@ EXPORTED_SYMBOLS = (
     "qmm_splitk_workspace_bytes",
     "qmm_linear_splitk",
     "qmm_linear_splitk_static",
+    "qmm_layernorm_modulate",
+    "qmm_set_sm_budget",
     "qmm_static_scratch_bytes",
 )
 
@@ -141,6 +143,10 @@ def load() -> ctypes.CDLL:
         lib.qmm_splitk_workspace_bytes.argtypes = [wp, i64, i32]
         lib.qmm_linear_splitk.restype = i32
         lib.qmm_linear_splitk.argtypes = [wp, vp, i64, ep, vp, i32, vp, ctypes.c_uint64, vp]
+        lib.qmm_set_sm_budget.restype = i32
+        lib.qmm_set_sm_budget.argtypes = [i32]
+        lib.qmm_layernorm_modulate.restype = i32
+        lib.qmm_layernorm_modulate.argtypes = [vp, i64, i64, vp, vp, ctypes.c_float, vp, vp]
         lib.qmm_linear_splitk_static.restype = i32
         lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
         lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64

@@ -60,6 +60,8 @@ uint32_t *device_error_word() {
     return g_err_addr[dev];
 }
 
+std::atomic<int> g_sm_budget{0};
+
 int sm_count() {
     const int dev = current_device();
     if (g_sm_count[dev] == 0) {
@@ -68,7 +70,8 @@ int sm_count() {
             n = 148;
         g_sm_count[dev] = n;
     }
-    return g_sm_count[dev];
+    const int budget = g_sm_budget.load(std::memory_order_relaxed);
+    return budget > 0 && budget < g_sm_count[dev] ? budget : g_sm_count[dev];
 }
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -96,6 +99,11 @@ int32_t qmm_abi_version(void) { return QMM_ABI_VERSION; }
 const char *qmm_last_error(void) { return qmm::t_last_error.c_str(); }
 
 uint64_t qmm_launch_count(void) { return qmm::g_launches.load(std::memory_order_relaxed); }
+
+int32_t qmm_set_sm_budget(int32_t sms) {
+    const int prev = qmm::g_sm_budget.exchange(sms > 0 ? sms : 0, std::memory_order_relaxed);
+    return prev;
+}
 
 qmm_status qmm_infer_layout(int64_t input, int64_t output, int64_t scales_rows,
                             int64_t scales_cols, int64_t packed_rows, int64_t packed_words,

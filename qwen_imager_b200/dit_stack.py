@@ -40,7 +40,8 @@ from typing import Callable, List, Optional
 import torch
 import torch.nn.functional as F
 
-from .quant import Affine, Linear
+from . import _lib
+from .quant import Affine, Linear, _stream_handle
 
 # ----------------------------------------------------------------- shapes
 
@@ -250,10 +251,18 @@ class _Span:
 
 
 class TensorParallel:
-    """Rank, world and the all-reduce of a tensor-parallel group."""
+    """Rank, world and the all-reduce of a tensor-parallel group.
 
-    def __init__(self, rank: int = 0, world: int = 1, group=None):
+    overlap_chunks > 1: the row-parallel linears run in that many token chunks
+    and each chunk's all-reduce is issued asynchronously as soon as the chunk's
+    GEMMs are enqueued, so it runs on NVLink while the next chunk computes;
+    the GEMMs then use `comm_sms` fewer SMs (qmm_set_sm_budget) so that the
+    collective's kernels have SMs to run on."""
+
+    def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 4, comm_sms: int = 16):
         self.rank, self.world, self.group = rank, world, group
+        self.overlap_chunks = overlap_chunks if world > 1 else 1
+        self.comm_sms = comm_sms
 
     @classmethod
     def from_env(cls):
@@ -266,6 +275,12 @@ class TensorParallel:
         if self.world > 1:
             import torch.distributed as dist
             dist.all_reduce(t, group=self.group)
+
+    def all_reduce_async(self, t: torch.Tensor):
+        """Enqueues the all-reduce after the current stream's work; the
+        returned handle's wait() makes the current stream wait for it."""
+        import torch.distributed as dist
+        return dist.all_reduce(t, group=self.group, async_op=True)
 
 
 class DitStack:
@@ -302,7 +317,8 @@ class DitStack:
             self._bufs = (key, torch.empty((m, 3 * dl), dtype=x.dtype, device=x.device),
                           torch.empty((m, dl), dtype=x.dtype, device=x.device),
                           torch.empty((m, cfg.ffn // w), dtype=x.dtype, device=x.device),
-                          torch.empty((2, cfg.mod_features), dtype=x.dtype, device=x.device))
+                          torch.empty((2, cfg.mod_features), dtype=x.dtype, device=x.device),
+                          torch.empty((m, cfg.hidden), dtype=x.dtype, device=x.device))
         return self._bufs[1:]
 
     def forward(self, x: torch.Tensor, temb: torch.Tensor, timers: Optional[Timers] = None) -> torch.Tensor:
@@ -313,45 +329,95 @@ class DitStack:
         mi = cfg.img_tokens
         if x.shape != (cfg.tokens, cfg.hidden):
             raise ValueError(f"hidden state {tuple(x.shape)} is not [{cfg.tokens}, {cfg.hidden}]")
-        qkv, attn, hid, mod = self._buffers(x)
+        qkv, attn, hid, mod, nbuf = self._buffers(x)
         rows = (slice(0, mi), slice(mi, cfg.tokens))
         dl = cfg.heads * cfg.head_dim // tp.world
         t_act = F.silu(temb.float()).to(x.dtype).reshape(1, cfg.hidden)
         last = tp.rank == 0
+        # Row-parallel linears and their all-reduce overlap on several ranks:
+        # one timing category for both.
+        rowpar = "linear" if tp.world == 1 else "rowpar_linear+all_reduce"
         for blk in self.blocks:
             with timers.span("linear"):
                 for s in range(2):
                     self.run_linear(blk[s].mod, t_act, out=mod[s:s + 1])
             chunks = [mod[s].view(6, cfg.hidden) for s in range(2)]
             with timers.span("other"):
-                n = [_modulate(x[rows[s]], chunks[s][0], chunks[s][1]) for s in range(2)]
+                n = [_modulate(x[rows[s]], chunks[s][0], chunks[s][1], nbuf[rows[s]]) for s in range(2)]
             with timers.span("linear"):
                 for s in range(2):
                     self.run_linear(blk[s].qkv, n[s], out=qkv[rows[s]])
             with timers.span("attention"):
                 self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
-            with timers.span("linear"):
-                for s in range(2):
-                    self.run_linear(blk[s].out, attn[rows[s]], gate=chunks[s][2],
-                                    residual=x[rows[s]] if last else None, out=x[rows[s]])
-            with timers.span("all_reduce"):
-                tp.all_reduce(x)
+            with timers.span(rowpar):
+                self._row_parallel([blk[0].out, blk[1].out], attn, [chunks[0][2], chunks[1][2]], x, last)
             with timers.span("other"):
-                n = [_modulate(x[rows[s]], chunks[s][3], chunks[s][4]) for s in range(2)]
+                n = [_modulate(x[rows[s]], chunks[s][3], chunks[s][4], nbuf[rows[s]]) for s in range(2)]
             with timers.span("linear"):
                 for s in range(2):
                     self.run_linear(blk[s].up, n[s], activation="gelu_tanh", out=hid[rows[s]])
-                for s in range(2):
-                    self.run_linear(blk[s].down, hid[rows[s]], gate=chunks[s][5],
-                                    residual=x[rows[s]] if last else None, out=x[rows[s]])
-            with timers.span("all_reduce"):
-                tp.all_reduce(x)
+            with timers.span(rowpar):
+                self._row_parallel([blk[0].down, blk[1].down], hid, [chunks[0][5], chunks[1][5]], x, last)
         return x
 
+    def _row_parallel(self, lins, inp, gates, x, last):
+        """x[rows of stream s] = gate_s * lin_s(inp[rows]) (+ x, rank 0), then
+        the sum over ranks; in token chunks with the all-reduce of each chunk
+        overlapping the next chunk's GEMMs when the group has several ranks."""
+        cfg, tp = self.cfg, self.tp
+        bounds = (0, cfg.img_tokens, cfg.tokens)
+        chunks = tp.overlap_chunks
+        if chunks <= 1:
+            for s in range(2):
+                r = slice(bounds[s], bounds[s + 1])
+                self.run_linear(lins[s], inp[r], gate=gates[s], residual=x[r] if last else None, out=x[r])
+            tp.all_reduce(x)
+            return
+        # Chunk edges on 192-token tiles of the joint token range.
+        step = -(-cfg.tokens // chunks)
+        step = -(-step // 192) * 192
+        edges = list(range(0, cfg.tokens, step)) + [cfg.tokens]
+        on_gpu = x.device.type == "cuda"
+        lib = _lib.load() if on_gpu else None
+        prev = lib.qmm_set_sm_budget(max(1, _sm_count(x.device) - tp.comm_sms)) if on_gpu else 0
+        try:
+            works = []
+            for a, b in zip(edges[:-1], edges[1:]):
+                for s in range(2):
+                    lo, hi = max(a, bounds[s]), min(b, bounds[s + 1])
+                    if lo < hi:
+                        r = slice(lo, hi)
+                        self.run_linear(lins[s], inp[r], gate=gates[s], residual=x[r] if last else None, out=x[r])
+                works.append(tp.all_reduce_async(x[a:b]))
+            for wk in works:
+                wk.wait()
+        finally:
+            if on_gpu:
+                lib.qmm_set_sm_budget(prev)
 
-def _modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
-    n = F.layer_norm(x, (x.shape[-1],), eps=1e-6)
-    return torch.addcmul(shift, n, scale + 1)
+
+_SM_COUNTS = {}
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNTS:
+        _SM_COUNTS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNTS[idx]
+
+
+def _modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """LayerNorm (eps 1e-6, no affine) * (1 + scale) + shift into `out`: one
+    fused CUDA kernel (qmm_layernorm_modulate) on the GPU; torch ops for the
+    CPU tensors of the host-logic tests."""
+    if x.device.type == "cuda":
+        rows, hidden = x.shape
+        _lib.check(_lib.load().qmm_layernorm_modulate(x.data_ptr(), rows, hidden, shift.data_ptr(), scale.data_ptr(),
+                                                      1e-6, out.data_ptr(), _stream_handle(x.device)))
+        return out
+    n = F.layer_norm(x.float(), (x.shape[-1],), eps=1e-6)
+    out.copy_(torch.addcmul(shift.float(), n, scale.float() + 1))
+    return out
 
 
 def _sdpa(qkv: torch.Tensor, out: torch.Tensor, heads: int, head_dim: int) -> None:

@@ -16,6 +16,7 @@ from qwen_imager_b200.dit_stack import (DitStack, StackConfig, TensorParallel, s
                                         stack_affine, stream_weights_full)
 from qmm_testutil import _bits16, _bits32, oracle_run_linear, rel_errors
 
+TP_MAX_REL = 2e-2
 SMALL = StackConfig(img_tokens=96, txt_tokens=32, bits=4, blocks=2, hidden=512, heads=4, head_dim=128,
                     ffn=1024)
 
@@ -127,5 +128,8 @@ def test_two_rank_gloo_stack_matches_one_rank(tmp_path):
     for r in range(2):
         y = torch.load(f"{path}.{r}")
         mx, mean = rel_errors(_bits16(y), ref.float().numpy())
-        assert mx <= 1e-2 and mean <= 1e-3, (r, mx, mean)
+        # Each rank rounds its partial output to bf16 before the all-reduce
+        # (two extra roundings per row-parallel layer, compounding over the
+        # blocks), so the bar on the largest element is twice the one-rank bar.
+        assert mx <= TP_MAX_REL and mean <= 1e-3, (r, mx, mean)
     assert torch.equal(torch.load(f"{path}.0"), torch.load(f"{path}.1"))

@@ -79,4 +79,5 @@ def test_stack_two_rank_nccl_matches_one_rank(tmp_path):
     mp.start_processes(_nccl_rank, args=(2, port, seed, path), nprocs=2, start_method="spawn")
     for r in range(2):
         mx, mean = rel_errors(_bits16(torch.load(f"{path}.{r}")), ref.float().cpu().numpy())
-        assert mx <= 1e-2 and mean <= 1e-3, (r, mx, mean)
+        # bf16 partial outputs before the all-reduce: see tests/test_dit_stack.py
+        assert mx <= 2e-2 and mean <= 1e-3, (r, mx, mean)
