@@ -325,7 +325,8 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                             tc_commit(&sempty[s]);
                         }
                     }
-                    __syncwarp();
+                    // (No __syncwarp here: the next block's wait ends in
+                    // __all_sync, which reconverges the warp.)
                     acc = 1;
                     issued = true;
                     if (++s == S) {
