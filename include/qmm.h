@@ -184,13 +184,18 @@ QMM_API qmm_status qmm_layernorm_modulate(const uint16_t *x, int64_t rows, int64
 
 /*
  * qmm_linear_splitk with the f32 scratch in a static device array of the
- * library (qmm_static_scratch_bytes() = 16 MiB per device) instead of a
- * caller workspace: allocates nothing.  No counterpart in quant.rs.
+ * library (qmm_static_scratch_bytes() = 16 MiB, held by every GPU that loads
+ * the library until exit) instead of a caller workspace: allocates nothing.
+ * For callers that cannot call cudaMalloc: plug-ins whose host owns all
+ * device memory and offers them no allocator, and paths that must not pay
+ * the device-wide synchronization of cudaMalloc/cudaFree.  No counterpart in
+ * quant.rs.
  *   - splits * m * n * 4 bytes must fit the scratch; larger requests return
  *     QMM_ERR_UNSUPPORTED before any launch;
- *   - nothing in the scratch must start at zero;
- *   - every call on a device uses the same scratch: calls that may overlap in
- *     time (other streams, threads) race, so order them on one stream;
+ *   - the scratch keeps the last call's contents; nothing in it must start
+ *     at zero;
+ *   - every call on a device uses the same scratch: calls that may overlap on
+ *     the GPU (other streams, threads) race, so order them on one stream;
  *   - the first call on a device resolves the scratch address with a runtime
  *     call; make it before any stream capture.
  */

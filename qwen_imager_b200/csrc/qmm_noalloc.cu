@@ -1,16 +1,26 @@
 // qmm_linear_splitk_static: the split-K GEMM with its f32 partial-sum scratch
-// in a file-scope device array instead of a caller-provided workspace, for
-// callers that cannot allocate device memory.  Nothing is allocated: the
-// scratch is part of the library's device image (one copy per device), and its
-// address is resolved once per device with cudaGetSymbolAddress.
+// in a file-scope device array instead of a caller-provided workspace.
+//
+// Who needs it: code that runs as a custom op or plug-in inside a host that
+// owns all device memory through its own pool and hands plug-ins no allocator
+// (an inference server's or framework's extension interface), where a private
+// cudaMalloc would fall outside the host's memory budget; and latency-critical
+// paths that must not pay the device-wide synchronization cudaMalloc/cudaFree
+// can imply.  This entry point allocates nothing: the scratch is part of the
+// library's device image, so every GPU that loads the library holds its 16 MiB
+// until the process exits.  In host code the array's name is only a host-side
+// stand-in, so its device address is resolved once per device, with that
+// device current, by cudaGetSymbolAddress, and that address is what the
+// kernels get.
 //
 // Contract (also stated in include/qmm.h):
 //   - at most kStaticScratchBytes (16 MiB) of scratch: splits * m * n * 4 bytes;
 //     larger requests fail with QMM_ERR_UNSUPPORTED before anything is launched;
-//   - nothing in the scratch has to start at zero: every split writes its
-//     whole partial tile before the reduction reads it;
+//   - the scratch keeps whatever the last call left in it; nothing has to
+//     start at zero, because every split writes its whole partial tile before
+//     the reduction reads it;
 //   - all calls on a device share the one scratch array, so calls that may
-//     overlap in time (different streams, host threads, processes sharing a
+//     overlap on the GPU (different streams, host threads, processes sharing a
 //     context) race; order them on one stream;
 //   - the first call on a device resolves the scratch address (a runtime
 //     call, not a stream operation): make it before any stream capture.

@@ -1,7 +1,10 @@
-"""The no-allocation split-K entry point (qmm_linear_splitk_static) against the
-caller-workspace one (qmm_linear_splitk): same kernels, same results, on two
-calls in a row; oversize requests are refused.  Kept in its own file, collected
-last, so it runs both alone and after every other test."""
+"""The no-allocation split-K entry point (qmm_linear_splitk_static), for
+callers that cannot call cudaMalloc (plug-ins whose host owns all device
+memory, paths that must not synchronize the device), against the
+caller-workspace entry point (qmm_linear_splitk): the same kernels give the
+same results on two calls in a row through the shared static scratch, and
+requests beyond the scratch's 16 MiB are refused.  Kept in its own file,
+collected last, so it runs both alone and after every other test."""
 import ctypes
 
 import numpy as np
