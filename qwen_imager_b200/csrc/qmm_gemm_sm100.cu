@@ -103,6 +103,10 @@ struct Params {
     int32_t m, n, k;
     int32_t group, groups, group_shift;
     int32_t w_tiles, tiles, num_units, splits, kbs;
+    // k-block pairs: dequantization sets 2j and 2j+1 fill A slots 2j, 2j+1
+    // and arrive on one barrier; the MMA warp waits once per two k-blocks.
+    // Requires 4 sets, 4 A slots, 1 CTA and an even kbs.
+    int32_t kpair;
     uint32_t *err;
 };
 
@@ -195,7 +199,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             mbar_init(&sempty[s], 1 + W::kPerSet);  // MMA commit + the dequant warps of the block's set
         }
         for (int a = 0; a < kASlots; ++a) {
-            mbar_init(&afull[a], kPairCtas * W::kPerSet);
+            mbar_init(&afull[a], kPairCtas * W::kPerSet * (p.kpair ? 2 : 1));
             mbar_init(&aempty[a], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -296,7 +300,46 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                 tc_fence_after_sync();
                 const uint32_t d = tmem + C::kAcc0 + b * T;
                 uint32_t acc = 0;
-                for (int kb = 0; kb < nkb; ++kb) {
+                if (!PAIR && p.kpair) {
+                    // Two k-blocks per A-slot-pair barrier (see Params::kpair);
+                    // afull implies full[s] and full[s + 1] as below.
+                    for (int kb = 0; kb < nkb; kb += 2) {
+                        const int pb = a >> 1;
+                        ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[pb], ph_a, p.err, kErrTimeoutMma));
+                        if (!ok) break;
+                        tc_fence_after_sync();
+                        const int s1 = s + 1 == S ? 0 : s + 1;
+                        if (lane_elect()) {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t atm = tmem + C::kASlot0 + (a + h) * 32;
+                                const uint64_t bdesc = bdesc0 + (uint64_t)(h ? s1 : s) * kBStep;
+#pragma unroll
+                                for (int kk = 0; kk < kBK / 16; ++kk) {
+                                    tc_mma_ts(d, atm + kk * 8, bdesc + (uint64_t)(kk * 2), C::kIdesc, acc);
+                                    acc = 1;
+                                }
+                            }
+                            tc_commit(&aempty[pb]);
+                            tc_commit(&sempty[s]);
+                            tc_commit(&sempty[s1]);
+                        }
+                        acc = 1;
+                        issued = true;
+                        for (int h = 0; h < 2; ++h) {
+                            if (++s == S) {
+                                s = 0;
+                                ph_s ^= 1;
+                            }
+                        }
+                        a += 2;
+                        if (a == kASlots) {
+                            a = 0;
+                            ph_a ^= 1;
+                        }
+                    }
+                }
+                for (int kb = 0; (PAIR || !p.kpair) && kb < nkb; ++kb) {
                     // 1-CTA: afull[a] implies full[s].  The dequantization warps
                     // that arrive on afull[a] first waited on full[s], the
                     // barrier the TMA copies of this stage (x tile and codes)
@@ -418,13 +461,14 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             else dequant_row_block<BITS, -1, 1>(pst, m0, m0, row, v, half);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
-            if (!mbar_wait<PAIR>(&aempty[a], ph_a ^ 1, p.err, kErrTimeoutDequant)) break;
+            const int ab = p.kpair ? (a >> 1) : a;  // the slot's barrier (shared by a slot pair)
+            if (!mbar_wait<PAIR>(&aempty[ab], ph_a ^ 1, p.err, kErrTimeoutDequant)) break;
             if constexpr (HALVES == 1) tmem_st_32x32b_x32(tcol + a * 32, v);
             else tmem_st_32x32b_x16(tcol + a * 32, v);
             tc_wait_st();
             tc_fence_before_sync();
             __syncwarp();
-            if (lane == 0) arrive_leader(&afull[a]);
+            if (lane == 0) arrive_leader(&afull[ab]);
             m0 = n0m;
             m1 = n1m;
             kb = nkb_i;
@@ -693,6 +737,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.splits = splits;
     p.kbs = (int32_t)(w.k / kBK / splits);
     p.num_units = p.tiles * splits;
+    p.kpair = (!PAIR && SETS == 4 && HALVES == 1 && C::kASlots == 4 && p.kbs % 2 == 0) ? 1 : 0;
     p.err = device_error_word();
     const int ctas = PAIR ? 2 : 1;
     const int units = (int)std::min<int64_t>(p.num_units, sm_count() / ctas);
