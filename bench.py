@@ -66,6 +66,8 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(STACK_WORKLOADS), default="ffn_up")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--overlap-chunks", type=int, default=1,
+                   help="dit_*: token chunks whose all-reduce overlaps the next chunk's GEMMs (1 = none)")
     a = p.parse_args()
     stack = a.workload in STACK_WORKLOADS
     if a.steps is None:
@@ -370,7 +372,7 @@ def run_stack(args, rank, world, device):
     from qwen_imager_b200.dit_stack import STACKS, DitStack, TensorParallel, Timers
 
     cfg = STACKS[args.workload]
-    tp = TensorParallel(rank, world)
+    tp = TensorParallel(rank, world, overlap_chunks=args.overlap_chunks)
     stack = DitStack.random(cfg, tp, seed=1, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(1234)  # the same hidden state and timestep on every rank
@@ -643,6 +645,7 @@ def main_stack(args, world, rank, local):
     config = {"workload": f"{args.workload}: {STACK_WORKLOADS[args.workload]}", "global_batch": 1,
               "tokens": cfg.tokens, "hidden": cfg.hidden, "blocks": cfg.blocks, "bits": cfg.bits, "group": cfg.group,
               "parallelism": f"tp{world} (column-parallel QKV/up, row-parallel out/down, NCCL all-reduce)",
+              "overlap_chunks": args.overlap_chunks,
               "l2": "weights of every step (GBs) far exceed L2 (no flush)"}
     common = {"metric": STACK_METRIC, "unit": "ms", "steps": args.steps, "warmup": args.warmup,
               "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "config": config}

@@ -253,13 +253,16 @@ class _Span:
 class TensorParallel:
     """Rank, world and the all-reduce of a tensor-parallel group.
 
-    overlap_chunks > 1: the row-parallel linears run in that many token chunks
+    overlap_chunks > 1 (opt-in; measured slower than one all-reduce per layer
+    on 8 B200 at the benchmark shapes, where four smaller collectives and
+    smaller GEMMs on fewer SMs cost more than the overlap hides): the
+    row-parallel linears run in that many token chunks
     and each chunk's all-reduce is issued asynchronously as soon as the chunk's
     GEMMs are enqueued, so it runs on NVLink while the next chunk computes;
     the GEMMs then use `comm_sms` fewer SMs (qmm_set_sm_budget) so that the
     collective's kernels have SMs to run on."""
 
-    def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 4, comm_sms: int = 16):
+    def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 1, comm_sms: int = 16):
         self.rank, self.world, self.group = rank, world, group
         self.overlap_chunks = overlap_chunks if world > 1 else 1
         self.comm_sms = comm_sms
