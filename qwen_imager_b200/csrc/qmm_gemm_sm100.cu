@@ -78,7 +78,7 @@ struct Cfg {
     static constexpr int kPOff = kXOff + kStages * kXStageBytes;
     static constexpr int kEOff = kPOff + kStages * kPStageBytes;
     static constexpr int kBarOff = kEOff + kEStageBytes;
-    static constexpr int kNumBars = 3 * kStages + 2 * 8 + 4 + 1;
+    static constexpr int kNumBars = 3 * kStages + 2 * 8 + 4 + 1 + 2;
     static constexpr int kTmemPtrOff = kBarOff + kNumBars * 8;
     static constexpr int kSmemBytes = kTmemPtrOff + 16 + 1024;  // + alignment slack
     static constexpr int kAcc0 = 0;                              // accumulator b at b*T
@@ -107,6 +107,9 @@ struct Params {
     // and arrive on one barrier; the MMA warp waits once per two k-blocks.
     // Requires 4 sets, 4 A slots, 1 CTA and an even kbs.
     int32_t kpair;
+    // The residual chunk of each write-back is loaded by TMA into the staging
+    // buffer (needs a residual, no split-K and n % 8 == 0).
+    int32_t res_tma;
     uint32_t *err;
 };
 
@@ -164,7 +167,8 @@ template <int BITS, int T, int SETS, int HALVES, bool PAIR>
 __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w,
-                    const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_out,
+                    const __grid_constant__ CUtensorMap tmap_res, const Params p) {
     using C = Cfg<BITS, T, PAIR>;
     using W = Warps<SETS, HALVES>;
     constexpr int S = C::kStages;
@@ -181,6 +185,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     uint64_t *acc_full = aempty + kASlots;                             // [2] tile accumulated
     uint64_t *acc_empty = acc_full + 2;                                // [2] tile drained
     uint64_t *drain = acc_empty + 2;                                   // error-path MMA drain
+    uint64_t *rfull = drain + 1;                                       // [2] residual chunk landed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kTmemPtrOff);
 
     const int warp = threadIdx.x >> 5;
@@ -207,6 +212,8 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             mbar_init(&acc_empty[b], kPairCtas * kEpiWarps);
         }
         mbar_init(drain, 1);
+        mbar_init(&rfull[0], 1);
+        mbar_init(&rfull[1], 1);
         fence_barrier_init();
     }
     if (warp == W::kMma) {
@@ -222,6 +229,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         tma_prefetch_desc(&tmap_x);
         tma_prefetch_desc(&tmap_w);
         tma_prefetch_desc(&tmap_out);
+        if (p.res_tma) tma_prefetch_desc(&tmap_res);
     }
     tc_fence_before_sync();
     __syncthreads();
@@ -489,6 +497,21 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int lt = 0;
         uint32_t chunk = 0;  // write-back chunks so far (staging buffer parity)
+        // Residual chunks by TMA: the chunk after the current one is requested
+        // into the other staging buffer as soon as the store that last read
+        // that buffer has finished reading it.
+        constexpr uint32_t kResBytes = 32 * kWRows * 2;
+        bool res_pending = false;  // a residual load is in flight (thread 0 of warp 0)
+        auto load_residual = [&](uint32_t ch, int wu_c, int c0_c) {
+            const int tile_c = wu_c % p.tiles;
+            const int n0_c = (tile_c % p.w_tiles) * kTileRows + (int)rank * kWRows;
+            const int m0_c = (tile_c / p.w_tiles) * T + c0_c;
+            uint64_t *bar = &rfull[ch & 1];
+            mbar_arrive_expect_tx(bar, kResBytes);
+            tma_load_2d(smem + C::kEOff + (ch & 1) * (C::kEStageBytes / 2), &tmap_res, bar, n0_c, m0_c);
+            res_pending = true;
+        };
+        if (p.res_tma && quad == 0 && lane == 0 && unit < p.num_units) load_residual(0, unit, 0);
         for (int wu = unit; wu < p.num_units; wu += nunits, ++lt) {
             const int b = lt & 1;
             const uint32_t u = lt >> 1;
@@ -545,6 +568,17 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     // may alias the residual; this chunk's residual elements
                     // are all read before its bulk stores are issued).
                     uint16_t *st16 = reinterpret_cast<uint16_t *>(stg);
+                    if (p.res_tma) {
+                        // This chunk's residual is in the staging buffer: read
+                        // it and overwrite it with the output in place.
+                        mbar_wait<PAIR>(&rfull[eb], (chunk >> 1) & 1, p.err, kErrTimeoutEpilogue);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            uint16_t &slot = st16[j * kWRows + quad * 32 + lane];
+                            slot = f32_to_bf16_bits(
+                                epilogue_value_rv(p.ep, fc, __uint_as_float(v[j]), bf16_bits_to_f32(slot)));
+                        }
+                    } else {
 #pragma unroll
                     for (int h = 0; h < 32; h += 8) {
                         float rv[8];
@@ -558,6 +592,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                         for (int j = 0; j < 8; ++j)
                             st16[(h + j) * kWRows + quad * 32 + lane] =
                                 f32_to_bf16_bits(epilogue_value_rv(p.ep, fc, __uint_as_float(v[h + j]), rv[j]));
+                    }
                     }
                 }
                 fence_proxy_async_smem();
@@ -575,11 +610,30 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     if (p.ws) tma_store_3d(&tmap_out, smem + C::kEOff, n0, (int32_t)mrow, split);
                     else tma_store_2d(&tmap_out, stg, n0, (int32_t)mrow);
                 }
-                if (quad == 0 && lane == 0) bulk_commit();
+                if (quad == 0 && lane == 0) {
+                    bulk_commit();
+                    res_pending = false;
+                    if (p.res_tma) {
+                        // Next chunk: in this tile, or the first of the next one.
+                        int wu_n = wu, c0_n = c0 + 32;
+                        if (c0_n >= T) {
+                            wu_n = wu + nunits;
+                            c0_n = 0;
+                        }
+                        if (wu_n < p.num_units) {
+                            bulk_wait_read<1>();  // the store of chunk - 1 read the other buffer
+                            load_residual(chunk + 1, wu_n, c0_n);
+                        }
+                    }
+                }
                 ++chunk;
             }
         }
-        if (quad == 0 && lane == 0) bulk_wait_all();  // the stores have landed before the CTA exits
+        if (quad == 0 && lane == 0) {
+            // On an early exit a prefetched residual chunk may still be landing.
+            if (res_pending) mbar_wait<PAIR>(&rfull[chunk & 1], (chunk >> 1) & 1, p.err, kErrTimeoutDrain);
+            bulk_wait_all();  // the stores have landed before the CTA exits
+        }
     }
 
     // ------------------------------------------------------------------ teardown
@@ -716,6 +770,14 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
         tout = tw;
     }
     if (s != QMM_OK) return s;
+    // Residual map: the epilogue loads residual chunks by TMA (same box as y).
+    CUtensorMap tres = tout;
+    const bool res_tma = ep.residual && splits == 1 && w.n % 8 == 0;
+    if (res_tma) {
+        s = make_map_2d(&tres, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ep.residual, (uint64_t)w.n, (uint64_t)m,
+                        (uint64_t)w.n * 2, kWRows, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (s != QMM_OK) return s;
+    }
 
     Params p;
     p.scales = w.scales;
@@ -738,6 +800,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.kbs = (int32_t)(w.k / kBK / splits);
     p.num_units = p.tiles * splits;
     p.kpair = (!PAIR && SETS == 4 && HALVES == 1 && C::kASlots == 4 && p.kbs % 2 == 0) ? 1 : 0;
+    p.res_tma = res_tma ? 1 : 0;
     p.err = device_error_word();
     const int ctas = PAIR ? 2 : 1;
     const int units = (int)std::min<int64_t>(p.num_units, sm_count() / ctas);
@@ -753,7 +816,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, tout, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, tout, tres, p);
     count_launch();
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
