@@ -8,8 +8,9 @@ on): the DiT FFN up projection, x bf16 [4352, 3072] ~ N(0,1) times 8-bit
 group-64 weights [12288, 3072] (W ~ N(0, 0.02), MLX affine quantization),
 plus the adaLN modulation GEMV of the same configuration, x [1, 3072] =
 SiLU(N(0,1)) times 4-bit weights [18432, 3072].  One step runs both linears
-once.  Data is synthetic and seeded; three weight/input sets (~290 MB, more
-than the 126 MB L2) rotate across steps so every step streams from HBM.
+once.  Data is synthetic and seeded.  Every linear rotates over at least three
+weight/input sets whose bytes together are at least twice the 126 MB L2
+(eight for the 32 MB GEMV), so every launch streams its operands from HBM.
 
 With N > 1 (torchrun, one process per GPU) every rank runs its own batch of
 the same workload (weak scaling: tokens are independent, no data-path
@@ -52,7 +53,8 @@ STACK_WORKLOADS = {
     "dit_1024_4bit": "60-block dual-stream DiT linear stack, 1024x1024 (4096 image + 256 text tokens), 4-bit",
     "dit_2048_8bit": "60-block dual-stream DiT linear stack, 2048x2048 (16384 image + 512 text tokens), 8-bit",
 }
-ROTATE = 3
+ROTATE = 3              # fewest sets a linear rotates over
+L2_BYTES = 126 * 2**20  # each linear's rotation covers at least twice this
 METRIC = "qmm TFLOP/s (quantized DiT linears, bf16 tensor cores)"
 STACK_METRIC = "DiT-stack step ms (60 blocks: quantized linears + joint attention + TP all-reduce)"
 
@@ -175,15 +177,26 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- our arm
+def layer_bytes(m, k, n, bits, ex):
+    """Bytes one launch reads and writes: codes, scales and offsets, x, y (and residual)."""
+    return n * k * bits // 8 + 2 * n * (k // 64) * 2 + 2 * m * k + 2 * m * n * (2 if ex.get("residual") else 1)
+
+
+def rotation(layer):
+    """Number of input sets a linear rotates over: its sets exceed twice the L2."""
+    return max(ROTATE, -(-2 * L2_BYTES // layer_bytes(*layer)))
+
+
 def build_sets(layers, seed, device):
+    """sets[li][r]: the r-th (Linear, x, residual, y) of layer li."""
     import torch
 
     from qwen_imager_b200.synthetic import gaussian, quantized_linear
 
     sets = []
-    for r in range(ROTATE):
+    for li, (m, k, n, bits, ex) in enumerate(layers):
         entry = []
-        for li, (m, k, n, bits, ex) in enumerate(layers):
+        for r in range(rotation(layers[li])):
             s = seed * 1000 + r * 10 + li
             lin = quantized_linear(n, k, bits, seed=s, bias_std=0.01 if ex.get("bias") else None, device=device)
             g = torch.Generator(device=device)
@@ -213,8 +226,9 @@ def run_ours(args, rank, world, device):
         import torch.distributed as tdist
 
     def step(i, only=None):
-        for li, (lin, x, res, y) in enumerate(sets[i % ROTATE]):
+        for li, rot in enumerate(sets):
             if only is None or only == li:
+                lin, x, res, y = rot[i % len(rot)]
                 lin.forward_fused(x, residual=res, out=y)
 
     for i in range(max(args.warmup, 3)):
@@ -280,7 +294,7 @@ def run_ours(args, rank, world, device):
     e2e = None
     if not args.no_e2e:
         host = []
-        for (lin, x, res, y) in sets[0]:
+        for (lin, x, res, y) in (rot[0] for rot in sets):
             hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
             hx.copy_(x)
             hr = None
@@ -293,7 +307,8 @@ def run_ours(args, rank, world, device):
         d2h = sum(hy.numel() * 2 for _, _, hy in host)
 
         def e2e_step(i):
-            for (lin, x, res, y), (hx, hr, hy) in zip(sets[i % ROTATE], host):
+            for rot, (hx, hr, hy) in zip(sets, host):
+                lin, x, res, y = rot[i % len(rot)]
                 x.copy_(hx, non_blocking=True)
                 if hr is not None:
                     res.copy_(hr, non_blocking=True)
@@ -586,7 +601,8 @@ def main():
     config = {"workload": f"{args.workload}: {desc}", "global_batch": world,
               "tokens_per_rank": max(l[0] for l in layers), "group": 64,
               "parallelism": f"dp{world} (independent token batches)",
-              "l2": f"{ROTATE} rotating weight/input sets larger than L2 (no flush)",
+              "l2": "per linear " + "/".join(str(rotation(l)) for l in layers)
+                    + " rotating weight/input sets, together at least 2x the 126 MB L2 (no flush)",
               "launch": "the K timed steps replayed as one CUDA graph; e2e through the eager public API"}
 
     if args.impl == "reference":

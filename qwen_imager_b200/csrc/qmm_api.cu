@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -75,6 +76,14 @@ int sm_count() {
 }
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool gemv_pdl_enabled() {
+    static const bool on = [] {
+        const char *v = getenv("QMM_GEMV_PDL");
+        return !(v && v[0] == '0' && v[1] == '\0');
+    }();
+    return on;
+}
 
 }  // namespace qmm
 

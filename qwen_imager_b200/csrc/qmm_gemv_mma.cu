@@ -25,6 +25,14 @@
 // even j, high nibbles (codes 1,3 | 5,7) for odd j.  About one instruction
 // per code instead of a multiply-add per code on the FMA pipe.
 //
+// Launch.  With programmatic dependent launch the next launch's CTAs take
+// each SM as soon as this grid's CTA there exits, instead of after the whole
+// grid drains and a new launch ramps up.  Before the grids it depends on have
+// completed, a CTA only prefetches its weight rows into L2 (a hint: nothing is
+// read into shared memory or registers); every read of codes, scales, x,
+// bias, gate, residual and every write of y comes after griddepcontrol.wait,
+// so weights or x written by the kernel just before are seen in full.
+//
 // Reference computation: image-forger src/quant.rs:105-113 (weights
 // dequantized to f32 as scale * q + offset, f32 accumulation); the products
 // x * (128 + q) are exact in f32.  Every wait is bounded (qmm_common.cuh).
@@ -63,6 +71,7 @@ struct Params {
     int32_t row_bytes, row_stride, nblocks;
     int32_t stage_bytes, meta_off;            // scales at meta_off, offsets after them
     int32_t xp_stride;                        // u32 words per staged token
+    int32_t prefetch;                         // launched as a programmatic dependent: prefetch rows to L2
     uint32_t *err;
 };
 
@@ -80,6 +89,51 @@ __device__ __forceinline__ void mma_bf16_m16n8k16(float (&d)[4], uint32_t a0, ui
 template <uint32_t SEL>
 __device__ __forceinline__ uint32_t code_pair(uint32_t nibbles) {
     return __byte_perm(nibbles, 0x43434343u, SEL);
+}
+
+// Stages x in MMA order (threads [0, nthreads) of the block, whole warps).
+// Entry (token, u, t, j, r) of xp holds x at codes c0 = 64u + 16t + 8(j/2) +
+// (j%2) + 4r and c0 + 2 of the token (low half c0).  One task per
+// (token, u, t) reads its 16 codes with two 16-byte loads and writes its 8
+// entries; the four tasks of a unit sum X_u with shuffles.  Token row m of xp
+// is zero: B fragments of lanes whose token is >= m read it.
+template <int MP>
+__device__ __forceinline__ void stage_x(const uint16_t *x, uint32_t *xp, float *xsum, int m, int k, int units,
+                                        int xp_stride, int tid, int nthreads) {
+    for (int i = tid; i < units * 32; i += nthreads) xp[(size_t)m * xp_stride + i] = 0u;
+    for (int i = tid; i < units * MP; i += nthreads)
+        if (i % MP >= m) xsum[i] = 0.0f;
+    const int tasks = m * units * 4;
+    const int tasks_rounded = (tasks + 31) & ~31;  // whole warps: the shuffles below see all lanes
+    for (int base = 0; base < tasks_rounded; base += nthreads) {
+        const int i = base + tid;
+        const bool act = i < tasks;
+        const int t = i & 3, ut = i >> 2;
+        const int tok = act ? ut / units : 0, u = act ? ut - tok * units : 0;
+        float sum = 0.0f;
+        if (act) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)tok * k + u * kUnit + 16 * t);
+            const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+            const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};  // codes 2i | 2i+1
+            uint32_t out[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int jj = e >> 1, r = e & 1;
+                const int c0 = 8 * (jj >> 1) + (jj & 1) + 4 * r, c1 = c0 + 2;
+                const uint32_t lo = (w[c0 >> 1] >> ((c0 & 1) * 16)) & 0xFFFFu;
+                const uint32_t hi = (w[c1 >> 1] >> ((c1 & 1) * 16)) & 0xFFFFu;
+                out[e] = lo | (hi << 16);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)tok * xp_stride + u * 32 + t * 8);
+            dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+            dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (act && t == 0) xsum[u * MP + tok] = sum;
+    }
 }
 
 // Shared memory (16-byte aligned regions):
@@ -103,6 +157,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
     uint64_t *pready = empty + kMaxStages;  // [2] consumer warps -> reducer
     uint64_t *pfree = pready + 2;           // [2] reducer -> consumer warps
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
@@ -121,6 +176,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
         // ----------------------------------------------------------- reducer
         // Block j's partials are in part[j & 1]; the (j >> 1)-th completion of
         // pready[j & 1] says every consumer warp has written its slice.
+        pdl_dependency_wait();  // bias, gate and residual may come from the previous kernel; y may be read by it
         bool rok = true;
         int j = 0;
         for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
@@ -147,6 +203,23 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 
     if (warp == W::kProducer) {
         // ---------------------------------------------------------- producer
+        if (p.prefetch) {
+            // Lane l prefetches this CTA's l-th block (codes, scales, offsets)
+            // while the previous grid may still run.
+            const int b = blockIdx.x + lane * gridDim.x;
+            if (b < p.nblocks) {
+                const int64_t row0 = (int64_t)b * p.rb;
+                const int rows = (int)(p.n - row0 < p.rb ? p.n - row0 : p.rb);
+                const uint32_t meta = (uint32_t)rows * (uint32_t)p.groups * 2u;
+                const uint8_t *src = p.packed + row0 * p.row_bytes;
+                const uint32_t bytes = (uint32_t)rows * (uint32_t)p.row_bytes;
+                for (uint32_t off = 0; off < bytes; off += 65536u)
+                    bulk_prefetch_l2(src + off, bytes - off < 65536u ? bytes - off : 65536u);
+                bulk_prefetch_l2(p.scales + row0 * p.groups, meta);
+                bulk_prefetch_l2(p.offsets + row0 * p.groups, meta);
+            }
+        }
+        pdl_dependency_wait();
         int j = 0;
         for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
             const int s = j % p.stages;
@@ -171,46 +244,9 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
     }
 
     // ------------------------------------------------- stage x in MMA order
-    // Entry (token, u, t, j, r) holds x at codes c0 = 64u + 16t + 8(j/2) +
-    // (j%2) + 4r and c0 + 2 of the token (low half c0).  One task per
-    // (token, u, t) reads its 16 codes with two 16-byte loads and writes its 8
-    // entries; the four tasks of a unit sum X_u with shuffles.  Token row m of
-    // xp is zero: B fragments of lanes whose token is >= m read it.
     const int consumer_threads = CW * 32;
-    for (int i = threadIdx.x; i < p.units * 32; i += consumer_threads) xp[(size_t)p.m * p.xp_stride + i] = 0u;
-    for (int i = threadIdx.x; i < p.units * MP; i += consumer_threads)
-        if (i % MP >= p.m) xsum[i] = 0.0f;
-    const int tasks = p.m * p.units * 4;
-    const int tasks_rounded = (tasks + 31) & ~31;  // whole warps: the shuffles below see all lanes
-    for (int base = 0; base < tasks_rounded; base += consumer_threads) {
-        const int i = base + (int)threadIdx.x;
-        const bool act = i < tasks;
-        const int t = i & 3, ut = i >> 2;
-        const int tok = act ? ut / p.units : 0, u = act ? ut - tok * p.units : 0;
-        float sum = 0.0f;
-        if (act) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.x + (size_t)tok * p.k + u * kUnit + 16 * t);
-            const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
-            const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};  // codes 2i | 2i+1
-            uint32_t out[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int jj = e >> 1, r = e & 1;
-                const int c0 = 8 * (jj >> 1) + (jj & 1) + 4 * r, c1 = c0 + 2;
-                const uint32_t lo = (w[c0 >> 1] >> ((c0 & 1) * 16)) & 0xFFFFu;
-                const uint32_t hi = (w[c1 >> 1] >> ((c1 & 1) * 16)) & 0xFFFFu;
-                out[e] = lo | (hi << 16);
-            }
-            uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)tok * p.xp_stride + u * 32 + t * 8);
-            dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-            dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if (act && t == 0) xsum[u * MP + tok] = sum;
-    }
+    pdl_dependency_wait();  // x may come from the previous kernel
+    stage_x<MP>(p.x, xp, xsum, p.m, p.k, p.units, p.xp_stride, threadIdx.x, consumer_threads);
     named_barrier(1, consumer_threads);
 
     // ---------------------------------------------------------- consumers
@@ -416,14 +452,27 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.meta_off = pl.meta_off;
     p.xp_stride = pl.xp_stride;
     p.err = device_error_word();
+    const bool pdl = gemv_pdl_enabled();
+    p.prefetch = pdl ? 1 : 0;
     const int grid = (int)std::min<int64_t>(p.nblocks, sm_count());
-    qmm_gemv_mma_kernel<MT, TPW, CW><<<grid, Warps<CW>::kThreads, pl.smem, st>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(Warps<CW>::kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_gemv_mma_kernel<MT, TPW, CW>, p);
     count_launch();
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "gemv (mma) launch");
 }
 
 }  // namespace gemvtc
+
 
 bool gemv_mma_supported(const qmm_weight &w, int64_t m) {
     if (w.bits != 4 || m < 1 || m > 16) return false;
@@ -431,7 +480,7 @@ bool gemv_mma_supported(const qmm_weight &w, int64_t m) {
     const int per = w.group / gemvtc::kUnit;
     if ((per & (per - 1)) != 0) return false;
     if (w.n % 8 != 0 || w.k > (1 << 20) || w.n > ((int64_t)1 << 31)) return false;
-    // Bulk copies of scale/offset blocks need 16-byte aligned sources.
+    // Scale/offset blocks are copied in 16-byte pieces.
     if ((reinterpret_cast<uintptr_t>(w.scales) | reinterpret_cast<uintptr_t>(w.biases)) & 15u) return false;
     gemvtc::Plan pl;
     return gemvtc::plan_for(w, m, pl);

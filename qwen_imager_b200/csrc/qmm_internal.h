@@ -23,6 +23,10 @@ int sm_count();
 // Counts kernel launches (exported through qmm_launch_count()).
 void count_launch(uint64_t n = 1);
 
+// Whether the streaming GEMV is launched as a programmatic dependent of the
+// previous kernel of its stream (on unless QMM_GEMV_PDL=0; read once).
+bool gemv_pdl_enabled();
+
 // Launchers.  Arguments are validated by the caller (qmm_api.cu).
 qmm_status launch_dequantize(const qmm_weight &w, void *dst, int32_t dtype, cudaStream_t st);
 

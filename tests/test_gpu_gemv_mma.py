@@ -66,3 +66,57 @@ def test_gemv_mma_fused_epilogue(oracle, activation, act_code, m):
     ref = oracle.epilogue_bf16(y, gate, residual, act_code)
     d = np.abs(oracle.bf16_to_f32(got) - oracle.bf16_to_f32(ref))
     assert d.max() <= np.abs(oracle.bf16_to_f32(ref)).max() * 2.0**-7
+
+
+def test_gemv_mma_waits_for_the_kernels_before_it(oracle):
+    """The GEMV is launched as a programmatic dependent of the kernel before it
+    and reads nothing that kernel may write until it has completed.  Here the
+    codes, scales, offsets and x are rewritten by elementwise kernels on the
+    same stream right before every launch, and every launch's residual is the
+    previous launch's output; each result must match the oracle for the data
+    of its own iteration."""
+    import torch
+
+    k, n, m, iters = 3072, 2048, 1, 8
+    packed0, scales0, offsets0, bias = random_layer(n, k, 4, 64, seed=70)
+    lin = make_linear(packed0, scales0, offsets0, bias, 4, 64)
+    a = lin.affine
+    data = []
+    for i in range(iters):
+        packed, scales, offsets, _ = random_layer(n, k, 4, 64, seed=71 + i, bias=False)
+        x = oracle.f32_to_bf16(np.cos(np.arange(k, dtype=np.float64) * (0.11 + 0.07 * i)).astype(np.float32)
+                               .reshape(m, k))
+        data.append((packed, scales, offsets, x))
+    dev = [(to_dev_u32_i32(p), to_dev_u16(s), to_dev_u16(o), to_dev_u16(x)) for p, s, o, x in data]
+    xbuf = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
+    residual0 = oracle.f32_to_bf16(np.linspace(-1.0, 1.0, m * n, dtype=np.float32).reshape(m, n))
+    prev = to_dev_u16(residual0)
+    outs = [torch.empty((m, n), dtype=torch.bfloat16, device="cuda") for _ in range(iters)]
+    torch.cuda.synchronize()
+    for i, (p, s, o, x) in enumerate(dev):
+        torch.add(p, 0, out=a.packed.view(torch.int32))  # kernels, not copies: the launch before the GEMV
+        torch.mul(s, 1.0, out=a.scales)
+        torch.mul(o, 1.0, out=a.offsets)
+        torch.mul(x, 1.0, out=xbuf)
+        lin.forward_fused(xbuf, residual=prev, out=outs[i], path=_lib.QMM_PATH_GEMV)
+        prev = outs[i]
+    torch.cuda.synchronize()
+    got = [from_dev(t) for t in outs]
+    for i, (packed, scales, offsets, x) in enumerate(data):
+        res = residual0 if i == 0 else got[i - 1]
+        y = oracle.linear_f32(x, packed, scales, offsets, 4, 64, bias)
+        ref = oracle.epilogue_bf16(y, None, res, 0)
+        d = np.abs(oracle.bf16_to_f32(got[i]) - oracle.bf16_to_f32(ref))
+        assert d.max() <= np.abs(oracle.bf16_to_f32(ref)).max() * 2.0**-7, (i, d.max())
+
+
+def to_dev_u32_i32(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).cuda()
+
+
+def from_dev(t):
+    import torch
+
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
