@@ -218,14 +218,6 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
-// L2 prefetch of a global range (16-byte aligned, size a multiple of 16).  A
-// hint only: nothing is consumed, so it may run before the grid's
-// dependencies have completed.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-                 : "memory");
-}
-
 // Programmatic dependent launch.  launch_dependents lets the next kernel of
 // the stream, if it was launched with programmatic stream serialization, be
 // scheduled once every CTA of this grid has issued it or exited;

@@ -4,8 +4,11 @@
 // HBM-bound: every packed byte is read once, so the kernel's job is to keep
 // the copy engine busy and spend as few instructions per code as possible.
 // One persistent CTA per SM.  A producer warp streams blocks of RB weight
-// rows (codes with one bulk copy per row into a bank-staggered row stride,
-// plus the block's scales and offsets) into a ring of shared-memory stages.
+// rows into a ring of shared-memory stages: the codes with one bulk copy per
+// quad of 4 consecutive rows (contiguous in memory) into quad slots 32 bytes
+// longer than the quad, plus the block's scales and offsets.  Per-row copies
+// (34 per 56 KB block) were bound by the copy queue, ~3000 cycles per block
+// per SM; a quad copy moves 4 rows at once.
 // Consumer warps split a block into tile groups x K slices and leave
 // per-slice partial sums in a double buffer; a reducer warp
 // sums the slices, applies the epilogue and stores y, so consumer warps never
@@ -21,15 +24,17 @@
 // permutation of its K index, so the codes are fed to the MMA in the order
 // they sit in the packed words and x is staged once, in shared memory, in the
 // matching order:  lane (g, t) of a warp holds words 2t and 2t+1 of the unit
-// for rows g and g+8; MMA j takes word j/2, low nibbles (codes 0,2 | 4,6) for
-// even j, high nibbles (codes 1,3 | 5,7) for odd j.  About one instruction
-// per code instead of a multiply-add per code on the FMA pipe.
+// for MMA rows g and g+8; MMA j takes word j/2, low nibbles (codes 0,2 | 4,6)
+// for even j, high nibbles (codes 1,3 | 5,7) for odd j.  About one
+// instruction per code instead of a multiply-add per code on the FMA pipe.
+// MMA row g of a 16-row tile is row g >> 2 of the tile's quad g & 3 and MMA
+// row g + 8 is row 2 + (g >> 2) of that quad: the 4 rows an 8-byte load phase
+// reads (g = 0..3 or 4..7) sit in different quads, whose slots start 32 bytes
+// apart modulo 128, so they hit disjoint banks.
 //
 // Launch.  With programmatic dependent launch the next launch's CTAs take
 // each SM as soon as this grid's CTA there exits, instead of after the whole
-// grid drains and a new launch ramps up.  Before the grids it depends on have
-// completed, a CTA only prefetches its weight rows into L2 (a hint: nothing is
-// read into shared memory or registers); every read of codes, scales, x,
+// grid drains and a new launch ramps up.  Every read of codes, scales, x,
 // bias, gate, residual and every write of y comes after griddepcontrol.wait,
 // so weights or x written by the kernel just before are seen in full.
 //
@@ -68,10 +73,9 @@ struct Params {
     int64_t n;
     int32_t k, m, groups, units, unit_shift;  // unit u lies in group u >> unit_shift
     int32_t rb, ks, upw, stages;              // rows per block, K slices, units per slice, ring depth
-    int32_t row_bytes, row_stride, nblocks;
+    int32_t row_bytes, quad_stride, nblocks;   // quad slot = 4 rows + 32 bytes
     int32_t stage_bytes, meta_off;            // scales at meta_off, offsets after them
     int32_t xp_stride;                        // u32 words per staged token
-    int32_t prefetch;                         // launched as a programmatic dependent: prefetch rows to L2
     uint32_t *err;
 };
 
@@ -137,7 +141,7 @@ __device__ __forceinline__ void stage_x(const uint16_t *x, uint32_t *xp, float *
 }
 
 // Shared memory (16-byte aligned regions):
-//   stages [stages][rb * row_stride codes | rb*groups scales | rb*groups offsets]
+//   stages [stages][rb / 4 quad slots of codes | rb*groups scales | rb*groups offsets]
 //   xp     [m + 1][units][4 lanes t][4 MMAs j][2] u32   x in MMA order (bf16 pairs); row m zero
 //   xsum   [units][MP] f32                            X_u per token (zero beyond m)
 //   part   [2][ks][rb][m] f32                         partial sums per K slice (ks = 16 warps)
@@ -203,22 +207,6 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 
     if (warp == W::kProducer) {
         // ---------------------------------------------------------- producer
-        if (p.prefetch) {
-            // Lane l prefetches this CTA's l-th block (codes, scales, offsets)
-            // while the previous grid may still run.
-            const int b = blockIdx.x + lane * gridDim.x;
-            if (b < p.nblocks) {
-                const int64_t row0 = (int64_t)b * p.rb;
-                const int rows = (int)(p.n - row0 < p.rb ? p.n - row0 : p.rb);
-                const uint32_t meta = (uint32_t)rows * (uint32_t)p.groups * 2u;
-                const uint8_t *src = p.packed + row0 * p.row_bytes;
-                const uint32_t bytes = (uint32_t)rows * (uint32_t)p.row_bytes;
-                for (uint32_t off = 0; off < bytes; off += 65536u)
-                    bulk_prefetch_l2(src + off, bytes - off < 65536u ? bytes - off : 65536u);
-                bulk_prefetch_l2(p.scales + row0 * p.groups, meta);
-                bulk_prefetch_l2(p.offsets + row0 * p.groups, meta);
-            }
-        }
         pdl_dependency_wait();
         int j = 0;
         for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
@@ -232,9 +220,9 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
             if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)rows * (uint32_t)p.row_bytes + 2u * meta);
             __syncwarp();
             uint8_t *st = stages + (size_t)s * p.stage_bytes;
-            for (int r = lane; r < rows; r += 32)
-                bulk_load(st + (size_t)r * p.row_stride, p.packed + (row0 + r) * p.row_bytes,
-                          (uint32_t)p.row_bytes, &full[s]);
+            for (int q = lane; q * 4 < rows; q += 32)  // rows is a multiple of 8 (n % 8 == 0)
+                bulk_load(st + (size_t)q * p.quad_stride, p.packed + (row0 + 4 * q) * p.row_bytes,
+                          4u * (uint32_t)p.row_bytes, &full[s]);
             if (lane == 0) bulk_load(st + p.meta_off, p.scales + row0 * p.groups, meta, &full[s]);
             if (lane == 1)
                 bulk_load(st + p.meta_off + (size_t)p.rb * p.groups * 2, p.offsets + row0 * p.groups, meta,
@@ -277,8 +265,8 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 #pragma unroll
             for (int tl = 0; tl < TPW; ++tl) acc[mt][tl][0] = acc[mt][tl][1] = make_float2(0.0f, 0.0f);
         if (ok) {
-            const uint8_t *rowp = st + (size_t)(tile0 * 16 + g) * p.row_stride + t * 8;
-            const size_t tile_bytes = (size_t)16 * p.row_stride, half_bytes = (size_t)8 * p.row_stride;
+            const uint8_t *rowp = st + (size_t)(tile0 * 4 + (g & 3)) * p.quad_stride + (size_t)(g >> 2) * p.row_bytes + t * 8;
+            const size_t tile_bytes = (size_t)4 * p.quad_stride, half_bytes = (size_t)2 * p.row_bytes;
 #pragma unroll 2
             for (int u = u0; u < u1; ++u) {
                 uint32_t bfr[MT][8];
@@ -324,7 +312,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
                 for (int tl = 0; tl < TPW; ++tl) {
 #pragma unroll
                     for (int hr = 0; hr < 2; ++hr) {
-                        const int row = (tile0 + tl) * 16 + hr * 8 + g;
+                        const int row = (tile0 + tl) * 16 + 4 * (g & 3) + (g >> 2) + 2 * hr;  // block row
                         const float sv = bf16_bits_to_f32(ssc[row * p.groups + gi]);
                         const float cv = fmaf(-128.0f, sv, bf16_bits_to_f32(sof[row * p.groups + gi]));
                         sc[tl][hr] = make_float2(sv, sv);
@@ -360,7 +348,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
             for (int tl = 0; tl < TPW; ++tl) {
 #pragma unroll
                 for (int hr = 0; hr < 2; ++hr) {
-                    const int row = (tile0 + tl) * 16 + hr * 8 + g;
+                    const int row = (tile0 + tl) * 16 + 4 * (g & 3) + (g >> 2) + 2 * hr;  // block row
                     if (t0 < p.m) pb[row * p.m + t0] = acc[mt][tl][hr].x;
                     if (t0 + 1 < p.m) pb[row * p.m + t0 + 1] = acc[mt][tl][hr].y;
                 }
@@ -372,7 +360,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 }
 
 struct Plan {
-    int rb, ks, tpw, cw, stages, row_stride, stage_bytes, meta_off, xp_stride;
+    int rb, ks, tpw, cw, stages, quad_stride, stage_bytes, meta_off, xp_stride;
     size_t smem;
 };
 
@@ -381,10 +369,9 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     const int mt = m <= 8 ? 1 : 2;
     const int64_t units = w.k / kUnit, groups = w.k / w.group;
     const int64_t row_bytes = w.k / 2;
-    // Row stride = 32 or 96 (mod 128) bytes: the 16 lanes of an 8-byte load
-    // phase (rows g = 0..3 of a tile) then hit disjoint banks.
-    const int64_t r128 = row_bytes % 128;
-    pl.row_stride = (int)(r128 == 32 || r128 == 96 ? row_bytes : row_bytes + 32);
+    // 4 * row_bytes is a multiple of 128 (k % 64 == 0): quad slots 32 bytes
+    // longer start 0, 32, 64, 96 bytes modulo 128 apart.
+    pl.quad_stride = (int)(4 * row_bytes + 32);
     pl.xp_stride = (int)(units * 32 + 4);  // +16 bytes: tokens start in different bank quads
     const size_t xs = (size_t)(m + 1) * pl.xp_stride * 4 + (size_t)units * 8 * mt * 4;
     for (int rb = 32; rb >= 16; rb /= 2) {
@@ -393,7 +380,7 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
         const int tpw = (pl.cw == 16 && rb == 32) ? 2 : 1;
         const int ks = pl.cw / ((rb / 16) / tpw);
         const int64_t meta = (int64_t)rb * groups * 2;
-        const int64_t stage = (int64_t)rb * pl.row_stride + 2 * meta;
+        const int64_t stage = (int64_t)(rb / 4) * pl.quad_stride + 2 * meta;
         const size_t fixed = xs + 2 * (size_t)ks * rb * m * 4 + 16 + (2 * kMaxStages + 4) * 8 + 64;
         int stages = kMaxStages;
         while (stages >= 2 && fixed + (size_t)stages * stage > kSmemLimit) --stages;
@@ -403,7 +390,7 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
         pl.tpw = tpw;
         pl.stages = stages;
         pl.stage_bytes = (int)stage;
-        pl.meta_off = rb * pl.row_stride;
+        pl.meta_off = (rb / 4) * pl.quad_stride;
         pl.smem = fixed + (size_t)stages * stage;
         return true;
     }
@@ -446,14 +433,13 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.upw = (p.units + pl.ks - 1) / pl.ks;
     p.stages = pl.stages;
     p.row_bytes = (int32_t)(w.k / 2);
-    p.row_stride = pl.row_stride;
+    p.quad_stride = pl.quad_stride;
     p.nblocks = (int32_t)((w.n + pl.rb - 1) / pl.rb);
     p.stage_bytes = pl.stage_bytes;
     p.meta_off = pl.meta_off;
     p.xp_stride = pl.xp_stride;
     p.err = device_error_word();
     const bool pdl = gemv_pdl_enabled();
-    p.prefetch = pdl ? 1 : 0;
     const int grid = (int)std::min<int64_t>(p.nblocks, sm_count());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
