@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *stages = smem;
     uint32_t *xp = reinterpret_cast<uint32_t *>(smem + (size_t)p.stages * p.stage_bytes);
-    float *xsum = reinterpret_cast<float *>(xp + (size_t)p.m * p.xp_stride);
+    float *xsum = reinterpret_cast<float *>(xp + (size_t)(p.m + 1) * p.xp_stride);  // after the zero row m
     float *part = xsum + (size_t)p.units * MP;
     uint64_t *full = reinterpret_cast<uint64_t *>(
         (reinterpret_cast<uintptr_t>(part + 2 * (size_t)p.ks * p.rb * p.m) + 15) & ~uintptr_t(15));
