@@ -1,30 +1,33 @@
 """Benchmark of the MLX affine quantized linear on B200 (one JSON line).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload ffn_up|linear_4bit|ffn_down|adaln_gemv|dit_1024_4bit|dit_2048_8bit]
+                  [--workload dit_2048_8bit|dit_1024_4bit|ffn_up|linear_4bit|ffn_down|adaln_gemv]
 
-Default workload (`ffn_up`, the configuration the headline metric is quoted
-on): the DiT FFN up projection, x bf16 [4352, 3072] ~ N(0,1) times 8-bit
-group-64 weights [12288, 3072] (W ~ N(0, 0.02), MLX affine quantization),
-plus the adaLN modulation GEMV of the same configuration, x [1, 3072] =
-SiLU(N(0,1)) times 4-bit weights [18432, 3072].  One step runs both linears
-once.  Data is synthetic and seeded.  Every linear rotates over at least three
-weight/input sets whose bytes together are at least twice the 126 MB L2
-(eight for the 32 MB GEMV), so every launch streams its operands from HBM.
+Default workload (`dit_2048_8bit`): one denoising step of the 60-block
+dual-stream DiT linear stack at 2048x2048 (16384 image + 512 text tokens,
+hidden 3072, 8-bit group-64 weights; qwen_imager_b200/dit_stack.py), in ms,
+tensor-parallel over the N ranks (strong scaling: the image is fixed, every
+rank holds 1/N of the weights).  On several ranks the stack runs in
+sequence-parallel form: after each row-parallel layer an NCCL reduce-scatter
+of the gated partials, one fused residual + LayerNorm + modulation kernel on
+the rank's tokens, and an NCCL all-gather before the next column-parallel
+layer.  The line carries a breakdown (quantized linears, attention,
+collectives, the rest), every distinct linear's per-launch time and
+roofline, an end-to-end time through host memory, and on N > 1 an untimed
+check of a small stack sharded over the N ranks against one rank
+(`tp_parity`).  Weights are random codes with N(0, 0.02)-sized scales; the
+hidden state is random.
 
-With N > 1 (torchrun, one process per GPU) every rank runs its own batch of
-the same workload (weak scaling: tokens are independent, no data-path
-collective); value is the total over ranks, timed as the max over ranks.
-
-The dit_* workloads time one denoising step of the 60-block dual-stream DiT
-linear stack (qwen_imager_b200/dit_stack.py) in ms, tensor-parallel over the
-N ranks (strong scaling: the image is fixed, every rank holds 1/N of the
-weights, two NCCL all-reduces of the joint hidden state per block), with a
-breakdown into quantized linears, attention, all-reduce and the rest.
+The kernel workloads (ffn_up, linear_4bit, ffn_down, adaln_gemv) time single
+quantized linears of the benchmark configurations in TFLOP/s; every linear
+rotates over at least three weight/input sets whose bytes together are at
+least twice the 126 MB L2, so every launch streams its operands from HBM.
+With N > 1 every rank runs its own batch (weak scaling, no collective).
 
 --impl reference times the reference's CPU path for the same workload on the
-host cores (the oracle's restatement: per-call f32 dequantization plus an f32
-GEMM), on a bounded row sample, rank 0 only.
+host cores (the oracle's restatement of src/quant.rs:105-113: per-call f32
+dequantization of the whole weight plus an f32 GEMM over all tokens), rank 0
+only; for the stack, one block timed piece by piece, x60.
 """
 from __future__ import annotations
 
@@ -56,24 +59,27 @@ STACK_WORKLOADS = {
 ROTATE = 3              # fewest sets a linear rotates over
 L2_BYTES = 126 * 2**20  # each linear's rotation covers at least twice this
 METRIC = "qmm TFLOP/s (quantized DiT linears, bf16 tensor cores)"
-STACK_METRIC = "DiT-stack step ms (60 blocks: quantized linears + joint attention + TP all-reduce)"
+STACK_METRIC = "DiT-stack step ms (60 blocks: quantized linears + joint attention + TP collectives)"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=None, help="default 300 (kernels), 5 (dit stacks)")
+    p.add_argument("--steps", type=int, default=None, help="default 300 (kernels), 10 (dit stacks)")
     p.add_argument("--warmup", type=int, default=None, help="default 5 (kernels), 3 (dit stacks)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(STACK_WORKLOADS), default="ffn_up")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(STACK_WORKLOADS), default="dit_2048_8bit")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-parity", action="store_true", help="dit_*: skip the untimed TP-vs-one-rank check (N > 1)")
+    p.add_argument("--replicated", action="store_true",
+                   help="dit_*: all-reduce the whole hidden state on every rank instead of the sequence-parallel form")
     p.add_argument("--overlap-chunks", type=int, default=1,
-                   help="dit_*: token chunks whose all-reduce overlaps the next chunk's GEMMs (1 = none)")
+                   help="dit_* --replicated: token chunks whose all-reduce overlaps the next chunk's GEMMs (1 = none)")
     a = p.parse_args()
     stack = a.workload in STACK_WORKLOADS
     if a.steps is None:
-        a.steps = 5 if stack else 300
+        a.steps = 10 if stack else 300
     if a.warmup is None:
         a.warmup = 3 if stack else 5
     return a
@@ -272,14 +278,16 @@ def run_ours(args, rank, world, device):
     elapsed = t0.elapsed_time(t1)
     # Per-layer launch time: the layer's K launches, same rotation, same stream.
     kernel_ms = []
-    for gl in layer_graphs:
-        gl.replay()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        gl.replay()
-        b.record()
-        torch.cuda.synchronize()
-        kernel_ms.append(a.elapsed_time(b) / args.steps)
+    layer_sampler = ClockSampler(torch.cuda.current_device())
+    with layer_sampler:
+        for gl in layer_graphs:
+            gl.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gl.replay()
+            b.record()
+            torch.cuda.synchronize()
+            kernel_ms.append(a.elapsed_time(b) / args.steps)
     if dist:
         tdist.barrier()
         t = torch.tensor([elapsed], device=device, dtype=torch.float64)
@@ -342,10 +350,9 @@ def run_ours(args, rank, world, device):
     dom = max(range(len(layers)), key=lambda li: 2.0 * layers[li][0] * layers[li][1] * layers[li][2])
     m, k, n, bits, _ = layers[dom]
     burst_tf, sustained_tf, hbm_gbs, peak_kind = measured_peaks()
-    # The GEMM is timed inside a loop of back-to-back launches (a long step at
-    # the 1 kW power cap): its denominator is the sustained bf16 figure; the
-    # fraction of the burst figure is reported beside it.
-    peak_tf = sustained_tf
+    # Burst or sustained denominator from the layer's own timed region: its
+    # length and the clock record taken while it ran.
+    peak_tf, tf_source = choose_peak(kernel_ms[dom] * args.steps * 1e-3, layer_sampler.summary())
     if m <= 16:
         alg_bytes = n * k * bits / 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
         achieved = alg_bytes / (kernel_ms[dom] * 1e-3) / 1e9
@@ -354,12 +361,12 @@ def run_ours(args, rank, world, device):
     else:
         achieved = 2.0 * m * n * k / (kernel_ms[dom] * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                "frac": round(achieved / peak_tf, 4), "frac_of_burst": round(achieved / burst_tf, 4)}
+                "frac": round(achieved / peak_tf, 4)}
     if m <= 16:
         roof["peak_source"] = f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"
     else:
-        roof["peak_source"] = (f"{peak_kind} sustained cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops_sustained); "
-                               f"burst {burst_tf}")
+        roof["peak_source"] = tf_source
+    roof["layer_clocks"] = layer_sampler.summary()
     roof["traffic"] = profile_traffic(args.workload)
     roof["kernel_ms"] = round(kernel_ms[dom], 5)
     per_layer = []
@@ -380,6 +387,154 @@ def run_ours(args, rank, world, device):
 
 
 # --------------------------------------------------------------- DiT stack arm
+def _layer_shapes(cfg, world):
+    """(name, stream, m, k, n, epilogue) of every distinct linear launch of one
+    block on one rank (column shards /world, row shards K/world)."""
+    h, f, d = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim
+    out = []
+    for s, m in ((0, cfg.img_tokens), (1, cfg.txt_tokens)):
+        tag = ("img", "txt")[s]
+        out += [(f"{tag}_qkv", s, m, h, 3 * d // world, "none"),
+                (f"{tag}_out", s, m, d // world, h, "gate" if world > 1 else "gate+bias+residual"),
+                (f"{tag}_up", s, m, h, f // world, "gelu_tanh"),
+                (f"{tag}_down", s, m, f // world, h, "gate" if world > 1 else "gate+bias+residual")]
+    out.append(("modulation", 0, 1, h, cfg.mod_features // world, "none"))
+    return out
+
+
+def time_stack_layers(stack, cfg, world, steps, device):
+    """Per-launch device time of each distinct linear of the stack on this
+    rank: for each, a CUDA graph of `steps` launches that walks over the
+    blocks' weights (each launch reads another block's weights from HBM),
+    timed with CUDA events on the capture stream."""
+    import torch
+
+    from qwen_imager_b200.quant import OWN_BIAS
+
+    bufs = stack._bufs[1]
+    h = cfg.hidden
+    srcs = {"qkv": bufs["nfull"], "out": bufs["attn"], "up": bufs["nfull"], "down": bufs["hid"]}
+    rows = (slice(0, cfg.img_tokens), slice(cfg.img_tokens, cfg.tokens))
+    gate = torch.ones((h,), dtype=torch.bfloat16, device=device)
+    bias = torch.zeros((h,), dtype=torch.bfloat16, device=device)
+    y = torch.empty((cfg.tokens, max(3 * cfg.heads * cfg.head_dim // world, cfg.ffn // world, h)),
+                    dtype=torch.bfloat16, device=device)
+    res = torch.zeros((cfg.tokens, h), dtype=torch.bfloat16, device=device)
+    t_act = torch.zeros((1, h), dtype=torch.bfloat16, device=device)
+    mod_out = torch.empty((1, cfg.mod_features // world), dtype=torch.bfloat16, device=device)
+    results = []
+    cap = torch.cuda.Stream(device)
+    for name, s, m, k, n, ep in _layer_shapes(cfg, world):
+        kind = name.split("_")[-1]
+
+        def launch(i, name=name, s=s, m=m, n=n, ep=ep, kind=kind):
+            blk = stack.blocks[i % len(stack.blocks)][s]
+            if name == "modulation":
+                blk.mod.forward_fused(t_act, out=mod_out)
+                return
+            lin = getattr(blk, kind)
+            x = srcs[kind][rows[s]]
+            out = y.view(-1)[: m * n].view(m, n)
+            kw = {}
+            if ep == "gelu_tanh":
+                kw["activation"] = "gelu_tanh"
+            elif ep.startswith("gate"):
+                kw["gate"] = gate
+                kw["bias"] = bias if "bias" in ep else None
+                if "residual" in ep:
+                    kw["residual"] = res[rows[s]]
+            lin.forward_fused(x, out=out, **kw)
+
+        for i in range(2):
+            launch(i)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(cap):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(steps):
+                    launch(i)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cap):
+            a.record(cap)
+            g.replay()
+            b.record(cap)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        del g
+        flops = 2.0 * m * n * k
+        entry = {"layer": name, "m": m, "k": k, "n": n, "bits": cfg.bits, "epilogue": ep,
+                 "launches_per_step": len(stack.blocks) * (1 if name != "modulation" else 2),
+                 "kernel_us": round(ms * 1e3, 2)}
+        if m <= 16:
+            byts = n * k * cfg.bits / 8 + n * (k // cfg.group) * 4 + m * k * 2 + m * n * 2
+            entry["GB/s"] = round(byts / (ms * 1e-3) / 1e9, 1)
+            entry["alg_bytes"] = int(byts)
+        else:
+            entry["TFLOP/s"] = round(flops / (ms * 1e-3) / 1e12, 1)
+            entry["alg_flops"] = flops
+        results.append(entry)
+    return results
+
+
+def choose_peak(region_s, clocks):
+    """Burst or sustained bf16 denominator for a kernel timed in a region of
+    `region_s` seconds with clock record `clocks`: sustained only when the
+    region lasts seconds and the record shows the power cap (or clocks held
+    well below the maximum); burst otherwise."""
+    burst, sustained, _hbm, kind = measured_peaks()
+    capped = "sw_power_cap" in (clocks.get("reasons") or [])
+    low = bool(clocks.get("sm_mhz") and clocks.get("sm_max_mhz") and clocks["sm_mhz"] < 0.9 * clocks["sm_max_mhz"])
+    if region_s >= 1.0 and (capped or low):
+        return sustained, f"{kind} sustained cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops_sustained): " \
+                          f"the timed region lasted {region_s:.1f} s under the power cap; burst {burst}"
+    return burst, f"{kind} burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops): the timed region lasted " \
+                  f"{region_s * 1e3:.0f} ms{' (power cap seen)' if capped else ''}; sustained {sustained}"
+
+
+TP_PARITY_CFG = dict(img_tokens=448, txt_tokens=64, blocks=2, hidden=1024, heads=8, head_dim=128, ffn=2048)
+
+
+def tp_parity(bits, rank, world, device):
+    """Untimed check on every rank: a small stack sharded over the N ranks
+    (sequence-parallel form, NCCL) against the same weights on this rank
+    alone; max|d| / max|ref| <= 1e-2 and mean|d| / max|ref| <= 1e-3."""
+    import torch
+    import torch.distributed as tdist
+
+    from qwen_imager_b200.dit_stack import DitStack, StackConfig, TensorParallel, stream_weights_full
+    from qwen_imager_b200.quant import Affine
+
+    cfg = StackConfig(bits=bits, **TP_PARITY_CFG)
+    g = torch.Generator().manual_seed(77)
+    full = [[stream_weights_full(cfg, g, "cpu") for _ in range(2)] for _ in range(cfg.blocks)]
+
+    def to_dev(a):
+        return Affine(packed=a.packed.to(device), scales=a.scales.to(device), offsets=a.offsets.to(device),
+                      bias=None if a.bias is None else a.bias.to(device), bits=a.bits, group=a.group, input=a.input)
+
+    full = [[{k: to_dev(v) for k, v in f.items()} for f in blk] for blk in full]
+    x = torch.randn((cfg.tokens, cfg.hidden), generator=g).to(torch.bfloat16).to(device)
+    temb = torch.randn((cfg.hidden,), generator=g).to(torch.bfloat16).to(device)
+    ref = DitStack.from_full(cfg, full, TensorParallel()).forward(x.clone(), temb).float()
+    got = DitStack.from_full(cfg, full, TensorParallel(rank, world)).forward(x.clone(), temb).float()
+    torch.cuda.synchronize()
+    d = (got - ref).abs()
+    scale = ref.abs().max()
+    errs = torch.tensor([float(d.max() / scale), float(d.mean() / scale), float(d.mean() / ref.abs().mean())],
+                        dtype=torch.float64, device=device)
+    tdist.all_reduce(errs, op=tdist.ReduceOp.MAX)
+    mx, mean, mm = (float(v) for v in errs.tolist())
+    return {"world": world, "form": "sequence-parallel (reduce-scatter + all-gather, NCCL bf16)",
+            "max_rel": round(mx, 6), "mean_rel": round(mean, 7), "mean_abs_over_mean_abs": round(mm, 6),
+            "bar": {"max_rel": 1e-2, "mean_rel": 1e-3}, "pass": bool(mx <= 1e-2 and mean <= 1e-3),
+            "normalised_by": "max|ref| (the reference test's metric); worst rank",
+            "config": f"{cfg.blocks} blocks, {cfg.img_tokens}+{cfg.txt_tokens} tokens, hidden {cfg.hidden}, "
+                      f"{cfg.heads} heads x {cfg.head_dim}, ffn {cfg.ffn}, {bits}-bit; TP{world} vs 1 rank"}
+
+
 def run_stack(args, rank, world, device):
     import torch
 
@@ -387,7 +542,8 @@ def run_stack(args, rank, world, device):
     from qwen_imager_b200.dit_stack import STACKS, DitStack, TensorParallel, Timers
 
     cfg = STACKS[args.workload]
-    tp = TensorParallel(rank, world, overlap_chunks=args.overlap_chunks)
+    tp = TensorParallel(rank, world, overlap_chunks=args.overlap_chunks,
+                        sequence_parallel=not args.replicated)
     stack = DitStack.random(cfg, tp, seed=1, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(1234)  # the same hidden state and timestep on every rank
@@ -428,6 +584,7 @@ def run_stack(args, rank, world, device):
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         elapsed = float(t.item())
     ms = elapsed / args.steps
+    clocks = sampler.summary()
 
     # One more step with CUDA events around every op category.
     timers = Timers(enabled=True)
@@ -438,16 +595,29 @@ def run_stack(args, rank, world, device):
     parts = {k: round(v, 3) for k, v in timers.totals_ms().items()}
     lin_flops = cfg.blocks * cfg.linear_flops_per_block()
     att_flops = cfg.blocks * cfg.attention_flops_per_block()
-    # On several ranks the row-parallel GEMMs overlap their all-reduce and are
-    # timed together with it: the achieved figure then counts that time too.
-    lin_ms = parts.get("linear", 0.0) + parts.get("rowpar_linear+all_reduce", 0.0)
-    burst_tf, peak_tf, _hbm, peak_kind = measured_peaks()
-    achieved = lin_flops / world / (lin_ms * 1e-3) / 1e12
-    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
-            "frac": round(achieved / peak_tf, 4), "frac_of_burst": round(achieved / burst_tf, 4), "traffic": None,
-            "kernel": "all quantized linears of one step on rank 0 (GEMMs + modulation GEMVs; on several ranks "
-                      "including the all-reduce time they do not hide)",
-            "peak_source": f"{peak_kind} sustained cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops_sustained)"}
+
+    # Per-launch time of every distinct linear on this rank; the roofline is
+    # that of the GEMM with the largest share of the step.
+    layer_sampler = ClockSampler(torch.cuda.current_device())
+    lt0 = time.perf_counter()
+    with layer_sampler:
+        layers = time_stack_layers(stack, cfg, world, max(args.steps, 8), device)
+    layer_region = time.perf_counter() - lt0
+    gemms = [e for e in layers if e["m"] > 16]
+    dom = max(gemms, key=lambda e: e["kernel_us"] * e["launches_per_step"])
+    peak, peak_source = choose_peak(layer_region / max(1, len(layers)), layer_sampler.summary())
+    achieved = dom["alg_flops"] / (dom["kernel_us"] * 1e-6) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
+            "kernel": f"{dom['layer']} GEMM {dom['m']}x{dom['k']}x{dom['n']} {cfg.bits}-bit ({dom['epilogue']}), "
+                      f"rank 0",
+            "kernel_ms": round(dom["kernel_us"] * 1e-3, 5), "peak_source": peak_source,
+            "layer_clocks": layer_sampler.summary()}
+    for e in layers:
+        if "TFLOP/s" in e:
+            e["frac_of_peak"] = round(e["TFLOP/s"] / peak, 4)
+        else:
+            e["hbm_frac"] = round(e["GB/s"] / measured_peaks()[2], 4)
 
     e2e = None
     if not args.no_e2e:
@@ -481,23 +651,39 @@ def run_stack(args, rank, world, device):
             tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
             e_ms = float(t.item())
         e2e = {"value": round(e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(hx.numel() * 2 + ht.numel() * 2),
-               "d2h_bytes_per_step": int(hy.numel() * 2)}
+               "d2h_bytes_per_step": int(hy.numel() * 2),
+               "what": "the public DitStack.forward with the hidden state and timestep copied in from pinned host "
+                       "memory and the new hidden state read back, every step (bytes per rank)"}
     if device_error(device):
         raise RuntimeError("device-side wait expired during the timed region")
+    parity = tp_parity(cfg.bits, rank, world, device) if (dist and not args.no_parity) else None
     breakdown = {"ms_" + k: v for k, v in parts.items()}
+    lin_ms = parts.get("linear", 0.0) + parts.get("rowpar_linear+all_reduce", 0.0)
     breakdown.update({
-        "linear_tflops_per_rank": round(achieved, 1),
+        "linear_tflops_per_rank": round(lin_flops / world / (lin_ms * 1e-3) / 1e12, 1) if lin_ms else None,
         "attention_tflops_per_rank": round(att_flops / world / (parts.get("attention", float("nan")) * 1e-3) / 1e12, 1),
         "linear_tflop_per_step": round(lin_flops / 1e12, 2), "attention_tflop_per_step": round(att_flops / 1e12, 2),
+        "collectives_per_step": (4 * cfg.blocks + 1 if tp.sequence_parallel else 2 * cfg.blocks) + (1 if dist else 0),
     })
     return {"value": round(ms, 3), "ms_per_step": round(ms, 3), "e2e": e2e, "roofline": roof,
-            "gpu_launches": int(launches), "breakdown": breakdown, "clocks": sampler.summary()}
+            "gpu_launches": int(launches), "breakdown": breakdown, "clocks": clocks, "layers": layers,
+            "tp_parity": parity, "form": "sequence-parallel" if tp.sequence_parallel else
+            ("replicated" if dist else "one rank")}
 
 
-def cpu_stack_reference(workload, steps):
-    """The reference CPU path for one block of the stack (every weight of both
-    streams dequantized to f32 per call, f32 GEMMs on a row sample scaled to
-    all rows, f32 attention of a query-row sample against all keys), times 60."""
+STACK_PIECES = ("modulation", "img_qkv", "img_out", "img_up", "img_down", "txt_linears", "attention", "norms")
+
+
+def cpu_stack_reference(workload, steps, warmup=0):
+    """The reference CPU path for the stack, timed on whole pieces of one
+    block: every linear runs as the reference's CPU path does
+    (src/quant.rs:105-113: the weight dequantized to f32 in full on every
+    call, an f32 GEMM over all its tokens, f32 bias, bf16 output), plus the
+    block's f32 joint attention over all tokens and its norms.  Each bench
+    step times one piece (rotating); every piece is timed at least once; the
+    block time is the sum of the pieces' medians and the step time that x 60
+    (the blocks are identical in cost).  Returns (step ms, cores, sample
+    description, mean seconds per bench step)."""
     import numpy as np
     import torch
 
@@ -511,48 +697,72 @@ def cpu_stack_reference(workload, steps):
     O.lib().oracle_set_threads(threads)
     rng = np.random.default_rng(7)
     h, f, d = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim
-    shapes = [(cfg.mod_features, h, 1), (3 * d, h, None), (h, d, None), (f, h, None), (h, f, None)]
-    layers = []
-    for n, k, m in shapes:
+    shapes = {"mod": (cfg.mod_features, h), "qkv": (3 * d, h), "out": (h, d), "up": (f, h), "down": (h, f)}
+    weights = {}
+    for name, (n, k) in shapes.items():
         w = rng.standard_normal((n, k), dtype=np.float32) * 0.02
-        layers.append((m, k) + O.quantize_affine(w, cfg.bits, 64))
-    rows = CPU_SAMPLE_ROWS
-    times = []
-    for _ in range(steps):
-        t_block = 0.0
-        for stream_tokens in (cfg.img_tokens, cfg.txt_tokens):
-            for (m, k, packed, scales, biases) in layers:
-                m = stream_tokens if m is None else m
-                r = min(rows, m)
-                x = O.f32_to_bf16(rng.standard_normal((r, k), dtype=np.float32))
-                t0 = time.perf_counter()
-                wf = O.dequantize_f32(packed, scales, biases, cfg.bits, 64)
-                t1 = time.perf_counter()
-                y = torch.from_numpy(O.bf16_to_f32(x)) @ torch.from_numpy(wf).T
-                O.f32_to_bf16(y.numpy())
-                t2 = time.perf_counter()
-                t_block += (t1 - t0) + (t2 - t1) * (m / r)
-        q = torch.randn((cfg.heads, rows, cfg.head_dim))
-        kv = torch.randn((2, cfg.heads, cfg.tokens, cfg.head_dim))
+        weights[name] = O.quantize_affine(w, cfg.bits, cfg.group)
+    bias = O.f32_to_bf16((rng.standard_normal(h) * 0.01).astype(np.float32))
+
+    def linear(name, m):
+        k = shapes[name][1]
+        x = O.f32_to_bf16(rng.standard_normal((m, k), dtype=np.float32))
+        packed, scales, offsets = weights[name]
         t0 = time.perf_counter()
-        torch.nn.functional.scaled_dot_product_attention(q, kv[0], kv[1])
-        t_block += (time.perf_counter() - t0) * (cfg.tokens / rows)
-        times.append(t_block * cfg.blocks)
-    t = statistics.median(times)
-    sample = (f"one block timed, x{cfg.blocks} blocks: both streams' weights dequantized to f32 in full "
-              f"(as the reference does per call), f32 GEMMs and f32 attention on {rows}-row samples scaled "
-              f"linearly to all rows; median of {steps}")
-    return t * 1e3, threads, sample
+        wf = O.dequantize_f32(packed, scales, offsets, cfg.bits, cfg.group)
+        y = torch.from_numpy(O.bf16_to_f32(x)) @ torch.from_numpy(wf).T
+        if name in ("out", "down"):
+            y += torch.from_numpy(O.bf16_to_f32(bias))
+        O.f32_to_bf16(y.numpy())
+        return time.perf_counter() - t0
+
+    def piece(name):
+        if name == "modulation":
+            return linear("mod", 1) + linear("mod", 1)
+        if name.startswith("img_"):
+            return linear(name[4:], cfg.img_tokens)
+        if name == "txt_linears":
+            return sum(linear(n, cfg.txt_tokens) for n in ("qkv", "out", "up", "down"))
+        if name == "attention":
+            q, k, v = (torch.randn((1, cfg.heads, cfg.tokens, cfg.head_dim)) for _ in range(3))
+            t0 = time.perf_counter()
+            torch.nn.functional.scaled_dot_product_attention(q, k, v)
+            return time.perf_counter() - t0
+        # norms: per stream two LayerNorm + modulation passes and two gated residual adds (f32)
+        xs = torch.randn((cfg.tokens, h))
+        sh, sc, gt = (torch.randn(h) for _ in range(3))
+        t0 = time.perf_counter()
+        for _ in range(2):
+            n = torch.nn.functional.layer_norm(xs, (h,), eps=1e-6) * (1 + sc) + sh
+            xs = xs + gt * n
+        return time.perf_counter() - t0
+
+    times = {p: [] for p in STACK_PIECES}
+    spent = []
+    for i in range(warmup + steps):
+        p = STACK_PIECES[i % len(STACK_PIECES)]
+        t = piece(p)
+        spent.append(t)
+        if i >= warmup:
+            times[p].append(t)
+    for p in STACK_PIECES:  # pieces the rotation did not reach
+        if not times[p]:
+            times[p].append(piece(p))
+    block_s = sum(statistics.median(v) for v in times.values())
+    sample = (f"one block of the stack timed piece by piece ({', '.join(STACK_PIECES)}; each bench step times "
+              f"one piece in rotation, every piece at least once), every linear over all its tokens with its "
+              f"weight dequantized to f32 in full per call; block time = sum of piece medians = "
+              f"{block_s:.2f} s, x{cfg.blocks} blocks")
+    return block_s * cfg.blocks * 1e3, threads, sample, statistics.mean(spent)
 
 
 # --------------------------------------------------------------------- CPU arm
-CPU_SAMPLE_ROWS = 128
-
-
-def cpu_reference(layers, seed, steps, warmup):
-    """Times the reference CPU path (oracle restatement) for one step of the
-    workload: full per-call dequantization of every weight plus the f32 GEMM on
-    a CPU_SAMPLE_ROWS-row sample of x, extrapolated linearly in rows."""
+def cpu_reference(layers, seed, steps, warmup, budget_s=120.0):
+    """Times the reference CPU path (the oracle's restatement of
+    src/quant.rs:105-113) for one step of the workload: every weight
+    dequantized to f32 in full per call, an f32 GEMM over all token rows, f32
+    bias, bf16 output.  Steps beyond what fits in `budget_s` seconds are not
+    run (the number timed is in the sample description)."""
     import numpy as np
     import torch
 
@@ -567,26 +777,31 @@ def cpu_reference(layers, seed, steps, warmup):
     for (m, k, n, bits, ex) in layers:
         w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02)
         packed, scales, biases = O.quantize_affine(w, bits, 64)
-        rows = min(m, CPU_SAMPLE_ROWS)
-        x = O.f32_to_bf16(rng.standard_normal((rows, k), dtype=np.float32))
-        data.append((m, rows, packed, scales, biases, bits, x))
-    times = []
-    for it in range(warmup + steps):
-        t_step = 0.0
-        for (m, rows, packed, scales, biases, bits, x) in data:
-            t0 = time.perf_counter()
+        x = O.f32_to_bf16(rng.standard_normal((m, k), dtype=np.float32))
+        b = O.f32_to_bf16((rng.standard_normal(n) * 0.01).astype(np.float32)) if ex.get("bias") else None
+        data.append((packed, scales, biases, bits, x, b))
+
+    def one_step():
+        t0 = time.perf_counter()
+        for (packed, scales, biases, bits, x, b) in data:
             wf = O.dequantize_f32(packed, scales, biases, bits, 64)
-            t1 = time.perf_counter()
             y = torch.from_numpy(O.bf16_to_f32(x)) @ torch.from_numpy(wf).T
+            if b is not None:
+                y += torch.from_numpy(O.bf16_to_f32(b))
             O.f32_to_bf16(y.numpy())
-            t2 = time.perf_counter()
-            t_step += (t1 - t0) + (t2 - t1) * (m / rows)
-        if it >= warmup:
-            times.append(t_step)
+        return time.perf_counter() - t0
+
+    first = one_step()
+    fit = max(1, int(budget_s / max(first, 1e-6)))
+    n_warm = min(max(warmup - 1, 0), fit // 4)
+    n_steps = max(1, min(steps, fit - n_warm))
+    for _ in range(n_warm):
+        one_step()
+    times = [one_step() for _ in range(n_steps)]
     t = statistics.median(times)
-    sample = (f"per step: every weight dequantized to f32 in full (as the reference does per call), "
-              f"f32 GEMM on {min(CPU_SAMPLE_ROWS, max(l[0] for l in layers))} of the token rows, GEMM time "
-              f"scaled linearly to all rows; median of {steps} steps")
+    sample = (f"per step: every weight dequantized to f32 in full (as the reference does per call), f32 GEMM over "
+              f"all {max(l[0] for l in layers)} token rows, bf16 output; median of {n_steps} steps"
+              + (f" (of {steps} asked; the rest did not fit {budget_s:.0f} s)" if n_steps < steps else ""))
     return step_flops(layers) / t / 1e12, t, threads, sample
 
 
@@ -643,7 +858,7 @@ def main():
            "gpu_launches": res["gpu_launches"], "clocks": res["clocks"], "layers": res["layers"]}
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            value, t, cores, sample = cpu_reference(layers, seed, 3, 1)
+            value, t, cores, sample = cpu_reference(layers, seed, 3, 1, budget_s=30.0)
             out["cpu_baseline"] = {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores,
                                    "kind": "port", "sample": sample}
         except Exception as exc:  # the CPU leg must not hide the GPU result
@@ -658,20 +873,27 @@ def main():
 def main_stack(args, world, rank, local):
     from qwen_imager_b200.dit_stack import STACKS
     cfg = STACKS[args.workload]
+    form = ("replicated hidden state, NCCL all-reduce after each row-parallel layer" if args.replicated else
+            "sequence-parallel: NCCL reduce-scatter after each row-parallel layer, fused residual + LayerNorm + "
+            "modulation on the local tokens, NCCL all-gather before each column-parallel layer")
     config = {"workload": f"{args.workload}: {STACK_WORKLOADS[args.workload]}", "global_batch": 1,
               "tokens": cfg.tokens, "hidden": cfg.hidden, "blocks": cfg.blocks, "bits": cfg.bits, "group": cfg.group,
-              "parallelism": f"tp{world} (column-parallel QKV/up, row-parallel out/down, NCCL all-reduce)",
+              "parallelism": f"tp{world} (column-parallel QKV/up/modulation, row-parallel out/down; {form})"
+                             if world > 1 else "tp1",
               "overlap_chunks": args.overlap_chunks,
-              "l2": "weights of every step (GBs) far exceed L2 (no flush)"}
+              "l2": "weights of every step (GBs) far exceed L2 (no flush); per-layer timings walk over the blocks' "
+                    "weights (inputs + weights of each launch > 126 MB)"}
     common = {"metric": STACK_METRIC, "unit": "ms", "steps": args.steps, "warmup": args.warmup,
               "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "config": config}
     if args.impl == "reference":
         if rank != 0:
             return
-        ms, cores, sample = cpu_stack_reference(args.workload, max(1, min(args.steps, 2)))
-        out = dict(common, value=round(ms, 1), impl="reference", n_gpus=args.gpus, ms_per_step=round(ms, 1),
-                   dtype="f32", data="synthetic",
-                   cpu_baseline={"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port", "sample": sample},
+        ms, cores, sample, per_step_s = cpu_stack_reference(args.workload, args.steps, args.warmup)
+        out = dict(common, value=round(ms, 1), impl="reference", n_gpus=args.gpus,
+                   ms_per_step=round(per_step_s * 1e3, 1), dtype="f32", data="synthetic",
+                   cpu_baseline={"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port",
+                                 "sample": sample + "; ms_per_step is the mean wall time of one bench step "
+                                                    "(one piece), value the whole denoising step"},
                    e2e={"value": round(ms, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(out), flush=True)
         return
@@ -689,10 +911,11 @@ def main_stack(args, world, rank, local):
         out = dict(common, value=res["value"], n_gpus=world, ms_per_step=res["ms_per_step"], dtype="bf16",
                    data="synthetic (random 4/8-bit codes with N(0,0.02)-sized scales; random hidden state)",
                    e2e=res["e2e"], roofline=res["roofline"], gpu_launches=res["gpu_launches"],
-                   clocks=res["clocks"], breakdown=res["breakdown"])
+                   clocks=res["clocks"], breakdown=res["breakdown"], layers=res["layers"],
+                   tp_parity=res["tp_parity"])
         if rank == 0 and world == 1 and not args.no_cpu:
             try:
-                ms, cores, sample = cpu_stack_reference(args.workload, 1)
+                ms, cores, sample, _ = cpu_stack_reference(args.workload, len(STACK_PIECES))
                 out["cpu_baseline"] = {"value": round(ms, 1), "unit": "ms", "cores": cores, "kind": "port",
                                        "sample": sample}
             except Exception as exc:

@@ -183,6 +183,26 @@ QMM_API qmm_status qmm_layernorm_modulate(const uint16_t *x, int64_t rows, int64
                                   uint16_t *out, void *stream);
 
 /*
+ * Residual update of a DiT hidden state and the next block input's LayerNorm
+ * + modulation, one pass per row (the sequence-parallel tensor-parallel
+ * stack, where `delta` is the reduce-scattered sum of the ranks' gated
+ * row-parallel partial outputs for this rank's rows):
+ *   x   = bf16(x + delta + gate * bias)                      f32, one rounding
+ *   out = bf16((x - mean) / sqrt(var + eps) * (1 + scale) + shift)   if out != NULL
+ * x, delta, out bf16 [rows, hidden]; bias, gate, shift, scale bf16 [hidden];
+ * bias (and gate, which multiplies only the bias) may be NULL; hidden one of
+ * 256, 512, 768, 1024, 1536, 2048, 3072, 4096; 16-byte aligned pointers;
+ * delta and out must not overlap x.  Replaces the residual add after the
+ * gated out/MLP projections and the norm before the next linear
+ * (src/dit.rs:88-93, src/dit.rs:50).
+ */
+QMM_API qmm_status qmm_residual_layernorm_modulate(uint16_t *x, int64_t rows, int64_t hidden,
+                                           const uint16_t *delta, const uint16_t *bias,
+                                           const uint16_t *gate, const uint16_t *shift,
+                                           const uint16_t *scale, float eps, uint16_t *out,
+                                           void *stream);
+
+/*
  * qmm_linear_splitk with the f32 scratch in a static device array of the
  * library (qmm_static_scratch_bytes() = 16 MiB, held by every GPU that loads
  * the library until exit) instead of a caller workspace: allocates nothing.
@@ -197,7 +217,10 @@ QMM_API qmm_status qmm_layernorm_modulate(const uint16_t *x, int64_t rows, int64
  *   - every call on a device uses the same scratch: calls that may overlap on
  *     the GPU (other streams, threads) race, so order them on one stream;
  *   - the first call on a device resolves the scratch address with a runtime
- *     call; make it before any stream capture.
+ *     call; make it before any stream capture;
+ *   - the address is kept for the life of the process: after cudaDeviceReset
+ *     (or anything else that destroys the device's primary context) do not
+ *     call this entry point again in that process.
  */
 QMM_API qmm_status qmm_linear_splitk_static(const qmm_weight *w, const uint16_t *x, int64_t m,
                                     const qmm_epilogue *ep, uint16_t *y, int32_t splits, void *stream);
@@ -219,6 +242,14 @@ QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
  * overlapping a row-parallel GEMM).  No counterpart in quant.rs.
  */
 QMM_API int32_t qmm_set_sm_budget(int32_t sms);
+
+/*
+ * Architecture of the library's device code, as the CUDA runtime reports it
+ * for one of its kernels (cudaFuncGetAttributes: binaryVersion and
+ * ptxVersion, major * 10 + minor; 100 for sm_100a).  Needs a CUDA device.
+ * No counterpart in quant.rs.
+ */
+QMM_API qmm_status qmm_binary_version(int32_t *binary_version, int32_t *ptx_version);
 
 /* Number of kernels this library has launched in the calling process (kernels
  * captured into a CUDA graph count once, at capture).  No counterpart in quant.rs. */

@@ -60,8 +60,10 @@ EXPORTED_SYMBOLS = (
     "qmm_linear_splitk",
     "qmm_linear_splitk_static",
     "qmm_layernorm_modulate",
+    "qmm_residual_layernorm_modulate",
     "qmm_set_sm_budget",
     "qmm_static_scratch_bytes",
+    "qmm_binary_version",
 )
 
 
@@ -147,10 +149,14 @@ def load() -> ctypes.CDLL:
         lib.qmm_set_sm_budget.argtypes = [i32]
         lib.qmm_layernorm_modulate.restype = i32
         lib.qmm_layernorm_modulate.argtypes = [vp, i64, i64, vp, vp, ctypes.c_float, vp, vp]
+        lib.qmm_residual_layernorm_modulate.restype = i32
+        lib.qmm_residual_layernorm_modulate.argtypes = [vp, i64, i64, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp]
         lib.qmm_linear_splitk_static.restype = i32
         lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
         lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64
         lib.qmm_static_scratch_bytes.argtypes = []
+        lib.qmm_binary_version.restype = i32
+        lib.qmm_binary_version.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32)]
         lib.qmm_device_error.restype = i32
         lib.qmm_device_error.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32)]
         _lib = lib

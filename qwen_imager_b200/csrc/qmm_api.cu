@@ -89,6 +89,10 @@ bool gemv_pdl_enabled() {
 
 using qmm::fail;
 
+// An empty kernel whose attributes report the architecture the library's
+// device code was built for (qmm_binary_version).
+__global__ void qmm_arch_probe_kernel() {}
+
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 static qmm_status check_device() {
@@ -108,6 +112,16 @@ int32_t qmm_abi_version(void) { return QMM_ABI_VERSION; }
 const char *qmm_last_error(void) { return qmm::t_last_error.c_str(); }
 
 uint64_t qmm_launch_count(void) { return qmm::g_launches.load(std::memory_order_relaxed); }
+
+qmm_status qmm_binary_version(int32_t *binary_version, int32_t *ptx_version) {
+    if (!binary_version || !ptx_version) return fail(QMM_ERR_INVALID_ARGUMENT, "null output pointer");
+    cudaFuncAttributes attr{};
+    cudaError_t e = cudaFuncGetAttributes(&attr, qmm_arch_probe_kernel);
+    if (e != cudaSuccess) return qmm::cuda_fail(e, "kernel attributes");
+    *binary_version = attr.binaryVersion;
+    *ptx_version = attr.ptxVersion;
+    return QMM_OK;
+}
 
 int32_t qmm_set_sm_budget(int32_t sms) {
     const int prev = qmm::g_sm_budget.exchange(sms > 0 ? sms : 0, std::memory_order_relaxed);

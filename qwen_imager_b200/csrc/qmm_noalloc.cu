@@ -23,7 +23,11 @@
 //     overlap on the GPU (different streams, host threads, processes sharing a
 //     context) race; order them on one stream;
 //   - the first call on a device resolves the scratch address (a runtime
-//     call, not a stream operation): make it before any stream capture.
+//     call, not a stream operation): make it before any stream capture;
+//   - the address is kept for the life of the process: after a
+//     cudaDeviceReset (or anything else that destroys the device's primary
+//     context) the library's device image is loaded anew and this entry point
+//     must not be called again in that process.
 #include <mutex>
 
 #include "qmm_internal.h"
@@ -67,6 +71,18 @@ uint64_t qmm_static_scratch_bytes(void) { return qmm::kStaticScratchBytes; }
 qmm_status qmm_linear_splitk_static(const qmm_weight *w, const uint16_t *x, int64_t m,
                                     const qmm_epilogue *ep, uint16_t *y, int32_t splits, void *stream) {
     if (!w) return qmm::fail(QMM_ERR_INVALID_ARGUMENT, "null weight");
+    if (splits < 1 || splits > 16)
+        return qmm::fail(QMM_ERR_INVALID_ARGUMENT, "split count %d is not in [1, 16]", splits);
+    if (m < 0 || w->n <= 0) return qmm::fail(QMM_ERR_BAD_SHAPE, "%lld tokens of %lld outputs", (long long)m,
+                                             (long long)w->n);
+    // splits * m * n * 4 bytes, compared without forming a product that could
+    // wrap: m * n must be at most the scratch's floats divided by the splits.
+    const uint64_t floats = qmm::kStaticScratchBytes / sizeof(float) / (uint64_t)splits;
+    if (splits > 1 && m > 0 && (uint64_t)m > floats / (uint64_t)w->n)
+        return qmm::fail(QMM_ERR_UNSUPPORTED,
+                         "split-k with %d splits of %lld x %lld needs more than the static scratch's %llu bytes "
+                         "(use qmm_linear_splitk with a caller workspace, or fewer splits)",
+                         splits, (long long)m, (long long)w->n, (unsigned long long)qmm::kStaticScratchBytes);
     const uint64_t need = qmm_splitk_workspace_bytes(w, m, splits);
     if (need > qmm::kStaticScratchBytes)
         return qmm::fail(QMM_ERR_UNSUPPORTED,

@@ -1,15 +1,16 @@
 """Tensor-parallel dual-stream MMDiT linear stack over the quantized linear.
 
 The caller of the quantized linear in image-forger is the DiT block
-(src/dit.rs:36-94): per block, a modulation linear on the timestep embedding
-(src/dit.rs:279, m = 1), q/k/v projections of the modulated, normalised
-hidden state (src/dit.rs:51-62), attention, the output projection with a
-gated residual (src/dit.rs:88-91) and a gated feed-forward residual
-(src/dit.rs:92-93, src/ops.rs:196-207).  This module runs that linear
-skeleton in the dual-stream, hidden-3072 form of the 60-block benchmark stack
-(image and text streams with their own weights, joint attention over both):
+(src/dit.rs:36-94): q/k/v projections of the modulated, normalised hidden
+state (src/dit.rs:51-62), attention, the output projection with a gated
+residual (src/dit.rs:88-91) and a gated feed-forward residual
+(src/dit.rs:92-93, src/ops.rs:196-207); the modulation linear runs once per
+denoising step on the timestep embedding, before the block loop
+(src/dit.rs:277-279, m = 1).  This module runs that linear skeleton in the
+dual-stream, hidden-3072 form of the 60-block benchmark stack (image and text
+streams with their own weights, joint attention over both):
 
-  mod   = Linear(3072 -> 18432)(silu(temb))          per stream, m = 1
+  mod   = Linear(3072 -> 18432)(silu(temb))          per block and stream, m = 1
   shift1, scale1, gate1, shift2, scale2, gate2 = mod.chunk(6)
   n     = layer_norm(x) * (1 + scale1) + shift1
   q,k,v = Linear(3072 -> 9216)(n)                     24 heads x 128
@@ -18,18 +19,30 @@ skeleton in the dual-stream, hidden-3072 form of the 60-block benchmark stack
   n     = layer_norm(x) * (1 + scale2) + shift2
   x     = x + gate2 * Linear(12288 -> 3072)(gelu_tanh(Linear(3072 -> 12288)(n)))
 
-Tensor parallelism over `world` ranks (one process per GPU):
+Every modulation depends only on the timestep, so all 2 x 60 modulation
+linears run first, column-parallel (each rank computes 1/world of every
+modulation's features) and one all-gather assembles them.
+
+Tensor parallelism over `world` ranks (one process per GPU), sequence-parallel
+form (the default on several ranks):
   * q/k/v and FFN-up are column-parallel: each rank holds 24/world heads
-    (its q, k and v columns, contiguous) and 12288/world FFN features;
+    (its q, k and v columns, contiguous) and 12288/world FFN features, and
+    reads the whole normalised input;
   * out and FFN-down are row-parallel: each rank holds a K slice, whole
-    scale groups, and computes a partial product;
-  * the partials meet in one NCCL all-reduce (sum, bf16) of the joint
-    [m_img + m_txt, 3072] hidden state per row-parallel layer.  Because
-    x + g * (sum_r P_r + b) = sum_r (g * P_r) + (x + g * b), every rank applies
-    the gate in its epilogue and only rank 0 adds the bias and the residual,
-    so the reduced buffer is the next hidden state with no extra pass;
-  * the modulation GEMV, the norms and the attention of a rank's heads need
-    no exchange (the GEMV is replicated: 32 MB per rank at 4-bit).
+    scale groups, and writes its gated partial product g * P_r of every
+    token (the gate is per feature, so g * sum_r P_r = sum_r g * P_r);
+  * a reduce-scatter (NCCL, bf16 sum) leaves each rank the summed partials of
+    its 1/world of the tokens; the hidden state itself is held that way,
+    sharded by tokens.  One fused kernel per rank adds the reduced partials
+    and g * bias to its rows and applies the next LayerNorm + modulation
+    (qmm_residual_layernorm_modulate), and an all-gather rebuilds the whole
+    normalised input of the next column-parallel linear.  The bytes on the
+    wire equal one all-reduce per row-parallel layer; the residual and norm
+    work is divided by world and no rank does more than another.
+The replicated form (sequence_parallel=False) keeps the whole hidden state on
+every rank and all-reduces it after each row-parallel layer, rank 0 folding
+the residual and bias into its GEMM epilogue; one rank always runs that form,
+with the residual fused into the GEMM epilogue.
 """
 from __future__ import annotations
 
@@ -41,7 +54,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .quant import Affine, Linear, _stream_handle
+from .quant import OWN_BIAS, Affine, Linear, _stream_handle
 
 # ----------------------------------------------------------------- shapes
 
@@ -130,14 +143,16 @@ def shard_output(a: Affine, rank: int, world: int, segments: int = 1) -> Affine:
     return _slice_affine(a, rows=rows)
 
 
-def shard_input(a: Affine, rank: int, world: int) -> Affine:
+def shard_input(a: Affine, rank: int, world: int, keep_bias: Optional[bool] = None) -> Affine:
     """Row-parallel shard: rank r keeps inputs [r*K/world, (r+1)*K/world) as
-    whole packed words and whole scale groups; the layer bias stays on rank 0
-    so the sum over ranks adds it once."""
+    whole packed words and whole scale groups.  By default the layer bias
+    stays on rank 0 so the sum over ranks adds it once; keep_bias=False drops
+    it on every rank (the caller adds it after the reduction)."""
     if a.input % world:
         raise ValueError(f"{a.input} inputs do not split over {world} ranks")
     kw = a.input // world
-    return _slice_affine(a, k0=rank * kw, k1=(rank + 1) * kw, keep_bias=(rank == 0))
+    keep = (rank == 0) if keep_bias is None else keep_bias
+    return _slice_affine(a, k0=rank * kw, k1=(rank + 1) * kw, keep_bias=keep)
 
 
 # ----------------------------------------------------------------- weights
@@ -163,11 +178,13 @@ def stack_affine(n: int, k: int, bits: int, *, generator: torch.Generator, group
 class StreamWeights:
     """One stream's linears in one block, already sharded for this rank."""
 
-    mod: Linear   # 3072 -> 18432, replicated
+    mod: Linear   # 3072 -> 18432 / world, column-parallel (rows [r F/w, (r+1) F/w) of the modulation)
     qkv: Linear   # 3072 -> 3 * heads/world * 128, column-parallel by heads
-    out: Linear   # heads/world * 128 -> 3072, row-parallel
+    out: Linear   # heads/world * 128 -> 3072, row-parallel (no bias of its own)
     up: Linear    # 3072 -> 12288/world, column-parallel
-    down: Linear  # 12288/world -> 3072, row-parallel
+    down: Linear  # 12288/world -> 3072, row-parallel (no bias of its own)
+    out_bias: Optional[torch.Tensor] = None   # bf16 [3072], the same on every rank
+    down_bias: Optional[torch.Tensor] = None  # bf16 [3072], the same on every rank
 
 
 def stream_weights_full(cfg: StackConfig, generator: torch.Generator, device) -> dict:
@@ -184,29 +201,36 @@ def stream_weights_full(cfg: StackConfig, generator: torch.Generator, device) ->
 
 def shard_stream(full: dict, rank: int, world: int) -> StreamWeights:
     return StreamWeights(
-        mod=Linear(affine=full["mod"]),
+        mod=Linear(affine=shard_output(full["mod"], rank, world)),
         qkv=Linear(affine=shard_output(full["qkv"], rank, world, segments=3)),
-        out=Linear(affine=shard_input(full["out"], rank, world)),
+        out=Linear(affine=shard_input(full["out"], rank, world, keep_bias=False)),
         up=Linear(affine=shard_output(full["up"], rank, world)),
-        down=Linear(affine=shard_input(full["down"], rank, world)),
+        down=Linear(affine=shard_input(full["down"], rank, world, keep_bias=False)),
+        out_bias=full["out"].bias,
+        down_bias=full["down"].bias,
     )
 
 
-def stream_weights_shard(cfg: StackConfig, rank: int, world: int, generator: torch.Generator,
-                         device) -> StreamWeights:
+def stream_weights_shard(cfg: StackConfig, rank: int, world: int, generator: torch.Generator, device,
+                         shared: torch.Generator) -> StreamWeights:
     """This rank's shard generated directly (the benchmark's 20B-parameter
     stack never exists unsharded): same shapes and statistics as sharding
-    `stream_weights_full`, different random draws."""
+    `stream_weights_full`, different random draws.  The row-parallel layers'
+    biases come from `shared`, a generator seeded alike on every rank, since
+    every rank adds them to its own tokens."""
     h, dl, fl = cfg.hidden, cfg.heads * cfg.head_dim // world, cfg.ffn // world
     g, b = cfg.group, cfg.bits
-    down = stack_affine(h, fl, b, generator=generator, group=g, bias=(rank == 0), device=device)
-    out = stack_affine(h, dl, b, generator=generator, group=g, bias=(rank == 0), device=device)
+    down = stack_affine(h, fl, b, generator=generator, group=g, bias=False, device=device)
+    out = stack_affine(h, dl, b, generator=generator, group=g, bias=False, device=device)
     return StreamWeights(
-        mod=Linear(affine=stack_affine(cfg.mod_features, h, b, generator=generator, group=g, device=device)),
+        mod=Linear(affine=stack_affine(cfg.mod_features // world, h, b, generator=generator, group=g,
+                                       device=device)),
         qkv=Linear(affine=stack_affine(3 * dl, h, b, generator=generator, group=g, device=device)),
         out=Linear(affine=out),
         up=Linear(affine=stack_affine(fl, h, b, generator=generator, group=g, device=device)),
         down=Linear(affine=down),
+        out_bias=(torch.randn((h,), generator=shared, device=device) * 0.01).to(torch.bfloat16),
+        down_bias=(torch.randn((h,), generator=shared, device=device) * 0.01).to(torch.bfloat16),
     )
 
 
@@ -215,8 +239,9 @@ def stream_weights_shard(cfg: StackConfig, rank: int, world: int, generator: tor
 RunLinear = Callable[..., torch.Tensor]
 
 
-def cuda_linear(lin: Linear, x: torch.Tensor, *, gate=None, residual=None, activation=None, out=None):
-    return lin.forward_fused(x, gate=gate, residual=residual, activation=activation, out=out)
+def cuda_linear(lin: Linear, x: torch.Tensor, *, gate=None, residual=None, activation=None, out=None,
+                bias=OWN_BIAS):
+    return lin.forward_fused(x, gate=gate, residual=residual, activation=activation, out=out, bias=bias)
 
 
 @dataclass
@@ -251,28 +276,40 @@ class _Span:
 
 
 class TensorParallel:
-    """Rank, world and the all-reduce of a tensor-parallel group.
+    """Rank, world and the collectives of a tensor-parallel group.
 
-    overlap_chunks > 1 (opt-in; measured slower than one all-reduce per layer
-    on 8 B200 at the benchmark shapes, where four smaller collectives and
-    smaller GEMMs on fewer SMs cost more than the overlap hides): the
-    row-parallel linears run in that many token chunks
-    and each chunk's all-reduce is issued asynchronously as soon as the chunk's
-    GEMMs are enqueued, so it runs on NVLink while the next chunk computes;
-    the GEMMs then use `comm_sms` fewer SMs (qmm_set_sm_budget) so that the
+    sequence_parallel (default): row-parallel outputs are reduce-scattered and
+    the hidden state is held sharded by tokens (see the module docstring);
+    otherwise they are all-reduced and every rank holds the whole hidden
+    state.
+
+    overlap_chunks > 1 (replicated form only; opt-in, measured slower than one
+    all-reduce per layer on 2 B200 at the benchmark shapes, where four smaller
+    collectives and smaller GEMMs on fewer SMs cost more than the overlap
+    hides): the row-parallel linears run in that many token chunks and each
+    chunk's all-reduce is issued asynchronously as soon as the chunk's GEMMs
+    are enqueued, so it runs on NVLink while the next chunk computes; the
+    GEMMs then use `comm_sms` fewer SMs (qmm_set_sm_budget) so that the
     collective's kernels have SMs to run on."""
 
-    def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 1, comm_sms: int = 16):
+    def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 1, comm_sms: int = 16,
+                 sequence_parallel: bool = True):
         self.rank, self.world, self.group = rank, world, group
         self.overlap_chunks = overlap_chunks if world > 1 else 1
         self.comm_sms = comm_sms
+        self.sequence_parallel = sequence_parallel and world > 1
 
     @classmethod
-    def from_env(cls):
+    def from_env(cls, **kw):
         import torch.distributed as dist
         if dist.is_available() and dist.is_initialized():
-            return cls(dist.get_rank(), dist.get_world_size())
-        return cls()
+            return cls(dist.get_rank(), dist.get_world_size(), **kw)
+        return cls(**kw)
+
+    def _native(self, t: torch.Tensor) -> bool:
+        """NCCL's tensor collectives for CUDA tensors; gloo (the CPU tests) lacks
+        reduce-scatter and gathers into a list."""
+        return t.device.type == "cuda"
 
     def all_reduce(self, t: torch.Tensor) -> None:
         if self.world > 1:
@@ -285,6 +322,31 @@ class TensorParallel:
         import torch.distributed as dist
         return dist.all_reduce(t, group=self.group, async_op=True)
 
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        """out [M / world, ...] = rows [rank M / world, (rank + 1) M / world) of
+        the sum over ranks of inp [M, ...]."""
+        if self.world == 1:
+            out.copy_(inp)
+            return
+        import torch.distributed as dist
+        if self._native(inp):
+            dist.reduce_scatter_tensor(out, inp, group=self.group)
+        else:
+            t = inp.clone()
+            dist.all_reduce(t, group=self.group)
+            out.copy_(t.chunk(self.world)[self.rank])
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        """out [world * L, ...] = the ranks' inp [L, ...] in rank order."""
+        if self.world == 1:
+            out.copy_(inp)
+            return
+        import torch.distributed as dist
+        if self._native(inp):
+            dist.all_gather_into_tensor(out, inp, group=self.group)
+        else:
+            dist.all_gather(list(out.chunk(self.world)), inp.contiguous(), group=self.group)
+
 
 class DitStack:
     """The 60-block dual-stream linear stack on one rank of a TP group."""
@@ -292,6 +354,8 @@ class DitStack:
     def __init__(self, cfg: StackConfig, blocks: List[List[StreamWeights]], tp: TensorParallel,
                  run_linear: RunLinear = cuda_linear, attention: Optional[Callable] = None):
         cfg.check_world(tp.world)
+        if tp.sequence_parallel and cfg.tokens % tp.world:
+            raise ValueError(f"{cfg.tokens} tokens do not split over {tp.world} ranks")
         self.cfg, self.blocks, self.tp = cfg, blocks, tp
         self.run_linear = run_linear
         self.attention = attention or _sdpa
@@ -301,8 +365,10 @@ class DitStack:
     def random(cls, cfg: StackConfig, tp: TensorParallel, seed: int = 0, device="cuda", blocks=None):
         g = torch.Generator(device=device)
         g.manual_seed(seed * 7919 + tp.rank)
+        shared = torch.Generator(device=device)
+        shared.manual_seed(seed * 7919 + 104729)
         nb = cfg.blocks if blocks is None else blocks
-        weights = [[stream_weights_shard(cfg, tp.rank, tp.world, g, device) for _ in range(2)]
+        weights = [[stream_weights_shard(cfg, tp.rank, tp.world, g, device, shared) for _ in range(2)]
                    for _ in range(nb)]
         return cls(cfg, weights, tp)
 
@@ -315,36 +381,139 @@ class DitStack:
         cfg, w = self.cfg, self.tp.world
         key = (x.shape[0], x.device, x.dtype)
         if self._bufs is None or self._bufs[0] != key:
-            m = x.shape[0]
+            m, h = x.shape[0], cfg.hidden
             dl = cfg.heads * cfg.head_dim // w
-            self._bufs = (key, torch.empty((m, 3 * dl), dtype=x.dtype, device=x.device),
-                          torch.empty((m, dl), dtype=x.dtype, device=x.device),
-                          torch.empty((m, cfg.ffn // w), dtype=x.dtype, device=x.device),
-                          torch.empty((2, cfg.mod_features), dtype=x.dtype, device=x.device),
-                          torch.empty((m, cfg.hidden), dtype=x.dtype, device=x.device))
-        return self._bufs[1:]
+            nb = len(self.blocks)
+            local = m // w if self.tp.sequence_parallel else m
+            e = lambda *shape: torch.empty(shape, dtype=x.dtype, device=x.device)  # noqa: E731
+            self._bufs = (key, dict(
+                qkv=e(m, 3 * dl), attn=e(m, dl), hid=e(m, cfg.ffn // w),
+                mod_local=e(2 * nb, cfg.mod_features // w), mod_all=e(w * 2 * nb, cfg.mod_features // w),
+                mods=e(2 * nb, cfg.mod_features),
+                nfull=e(m, h),            # normalised input of the column-parallel linears
+                part=e(m, h),             # gated row-parallel partials (sequence-parallel form)
+                xl=e(local, h), nl=e(local, h), red=e(local, h)))
+        return self._bufs[1]
 
-    def forward(self, x: torch.Tensor, temb: torch.Tensor, timers: Optional[Timers] = None) -> torch.Tensor:
-        """x: bf16 [img_tokens + txt_tokens, hidden] (image rows first), updated
-        in place and returned; temb: bf16 [hidden] timestep embedding."""
+    def modulations(self, temb: torch.Tensor, timers: Optional["Timers"] = None) -> torch.Tensor:
+        """All modulations of the step, bf16 [blocks, 2 streams, 6, hidden]:
+        each rank runs its column shard of the 2 x blocks modulation linears
+        (silu(temb) at m = 1, the streaming GEMV) and an all-gather assembles
+        the features."""
         cfg, tp = self.cfg, self.tp
         timers = timers or Timers()
-        mi = cfg.img_tokens
+        if self._bufs is None:
+            raise RuntimeError("modulations() runs inside forward(), which sizes the buffers")
+        bufs = self._bufs[1]
+        nb = len(self.blocks)
+        t_act = F.silu(temb.float()).to(torch.bfloat16).reshape(1, cfg.hidden)
+        loc = bufs["mod_local"]
+        with timers.span("linear"):
+            for b, blk in enumerate(self.blocks):
+                for s in range(2):
+                    self.run_linear(blk[s].mod, t_act, out=loc[2 * b + s:2 * b + s + 1])
+        if tp.world == 1:
+            return loc.view(nb, 2, 6, cfg.hidden)
+        with timers.span("comm"):
+            tp.all_gather(bufs["mod_all"], loc)
+        mods = bufs["mods"]
+        fl = cfg.mod_features // tp.world
+        mods.view(2 * nb, tp.world, fl).copy_(bufs["mod_all"].view(tp.world, 2 * nb, fl).transpose(0, 1))
+        return mods.view(nb, 2, 6, cfg.hidden)
+
+    def forward(self, x: torch.Tensor, temb: torch.Tensor, timers: Optional["Timers"] = None) -> torch.Tensor:
+        """x: bf16 [img_tokens + txt_tokens, hidden] (image rows first), updated
+        in place and returned; temb: bf16 [hidden] timestep embedding.  Every
+        rank passes the same x and temb and gets the whole new hidden state."""
+        cfg = self.cfg
+        timers = timers or Timers()
         if x.shape != (cfg.tokens, cfg.hidden):
             raise ValueError(f"hidden state {tuple(x.shape)} is not [{cfg.tokens}, {cfg.hidden}]")
-        qkv, attn, hid, mod, nbuf = self._buffers(x)
-        rows = (slice(0, mi), slice(mi, cfg.tokens))
+        self._buffers(x)
+        mods = self.modulations(temb, timers)
+        if self.tp.sequence_parallel:
+            return self._forward_sequence_parallel(x, mods, timers)
+        return self._forward_replicated(x, mods, timers)
+
+    def _stream_rows(self, lo: int, hi: int):
+        """(slice of [lo, hi) relative to lo, stream) for the stream segments of token rows [lo, hi)."""
+        bounds = (0, self.cfg.img_tokens, self.cfg.tokens)
+        out = []
+        for s in range(2):
+            a, b = max(lo, bounds[s]), min(hi, bounds[s + 1])
+            if a < b:
+                out.append((slice(a - lo, b - lo), s))
+        return out
+
+    def _forward_sequence_parallel(self, x, mods, timers):
+        cfg, tp = self.cfg, self.tp
+        bufs = self._bufs[1]
+        qkv, attn, hid, part = bufs["qkv"], bufs["attn"], bufs["hid"], bufs["part"]
+        nfull, xl, nl, red = bufs["nfull"], bufs["xl"], bufs["nl"], bufs["red"]
+        local = cfg.tokens // tp.world
+        lo = tp.rank * local
+        segs = self._stream_rows(lo, lo + local)
+        rows = (slice(0, cfg.img_tokens), slice(cfg.img_tokens, cfg.tokens))
         dl = cfg.heads * cfg.head_dim // tp.world
-        t_act = F.silu(temb.float()).to(x.dtype).reshape(1, cfg.hidden)
-        last = tp.rank == 0
-        # Row-parallel linears and their all-reduce overlap on several ranks:
-        # one timing category for both.
-        rowpar = "linear" if tp.world == 1 else "rowpar_linear+all_reduce"
-        for blk in self.blocks:
+        xl.copy_(x[lo:lo + local])
+        with timers.span("other"):
+            for r, s in segs:
+                _modulate(xl[r], mods[0, s, 0], mods[0, s, 1], nl[r])
+        with timers.span("comm"):
+            tp.all_gather(nfull, nl)
+        nb = len(self.blocks)
+        for b, blk in enumerate(self.blocks):
+            m = mods[b]
             with timers.span("linear"):
                 for s in range(2):
-                    self.run_linear(blk[s].mod, t_act, out=mod[s:s + 1])
-            chunks = [mod[s].view(6, cfg.hidden) for s in range(2)]
+                    self.run_linear(blk[s].qkv, nfull[rows[s]], out=qkv[rows[s]])
+            with timers.span("attention"):
+                self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
+            with timers.span("linear"):
+                for s in range(2):
+                    self.run_linear(blk[s].out, attn[rows[s]], gate=m[s, 2], bias=None, out=part[rows[s]])
+            with timers.span("comm"):
+                tp.reduce_scatter(red, part)
+            with timers.span("other"):
+                for r, s in segs:
+                    _residual_modulate(xl[r], red[r], blk[s].out_bias, m[s, 2], m[s, 3], m[s, 4], nl[r])
+            with timers.span("comm"):
+                tp.all_gather(nfull, nl)
+            with timers.span("linear"):
+                for s in range(2):
+                    self.run_linear(blk[s].up, nfull[rows[s]], activation="gelu_tanh", out=hid[rows[s]])
+                for s in range(2):
+                    self.run_linear(blk[s].down, hid[rows[s]], gate=m[s, 5], bias=None, out=part[rows[s]])
+            with timers.span("comm"):
+                tp.reduce_scatter(red, part)
+            last = b + 1 == nb
+            with timers.span("other"):
+                for r, s in segs:
+                    if last:
+                        _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], None, None, None)
+                    else:
+                        _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], mods[b + 1, s, 0],
+                                           mods[b + 1, s, 1], nl[r])
+            if not last:
+                with timers.span("comm"):
+                    tp.all_gather(nfull, nl)
+        with timers.span("comm"):
+            tp.all_gather(x, xl)
+        return x
+
+    def _forward_replicated(self, x, mods, timers):
+        cfg, tp = self.cfg, self.tp
+        bufs = self._bufs[1]
+        qkv, attn, hid, nbuf = bufs["qkv"], bufs["attn"], bufs["hid"], bufs["nfull"]
+        mi = cfg.img_tokens
+        rows = (slice(0, mi), slice(mi, cfg.tokens))
+        dl = cfg.heads * cfg.head_dim // tp.world
+        first = tp.rank == 0
+        # On several ranks the row-parallel linears and their all-reduce are
+        # one timing category (they overlap when chunked).
+        rowpar = "linear" if tp.world == 1 else "rowpar_linear+all_reduce"
+        for b, blk in enumerate(self.blocks):
+            chunks = mods[b]
             with timers.span("other"):
                 n = [_modulate(x[rows[s]], chunks[s][0], chunks[s][1], nbuf[rows[s]]) for s in range(2)]
             with timers.span("linear"):
@@ -353,27 +522,34 @@ class DitStack:
             with timers.span("attention"):
                 self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
             with timers.span(rowpar):
-                self._row_parallel([blk[0].out, blk[1].out], attn, [chunks[0][2], chunks[1][2]], x, last)
+                self._row_parallel([blk[0].out, blk[1].out], [blk[0].out_bias, blk[1].out_bias], attn,
+                                   [chunks[0][2], chunks[1][2]], x, first)
             with timers.span("other"):
                 n = [_modulate(x[rows[s]], chunks[s][3], chunks[s][4], nbuf[rows[s]]) for s in range(2)]
             with timers.span("linear"):
                 for s in range(2):
                     self.run_linear(blk[s].up, n[s], activation="gelu_tanh", out=hid[rows[s]])
             with timers.span(rowpar):
-                self._row_parallel([blk[0].down, blk[1].down], hid, [chunks[0][5], chunks[1][5]], x, last)
+                self._row_parallel([blk[0].down, blk[1].down], [blk[0].down_bias, blk[1].down_bias], hid,
+                                   [chunks[0][5], chunks[1][5]], x, first)
         return x
 
-    def _row_parallel(self, lins, inp, gates, x, last):
-        """x[rows of stream s] = gate_s * lin_s(inp[rows]) (+ x, rank 0), then
-        the sum over ranks; in token chunks with the all-reduce of each chunk
-        overlapping the next chunk's GEMMs when the group has several ranks."""
+    def _row_parallel(self, lins, biases, inp, gates, x, first):
+        """x[rows of stream s] = gate_s * (lin_s(inp[rows]) + bias_s) + x on rank
+        0, gate_s * lin_s(inp[rows]) elsewhere, then the sum over ranks; in
+        token chunks with the all-reduce of each chunk overlapping the next
+        chunk's GEMMs when overlap_chunks > 1."""
         cfg, tp = self.cfg, self.tp
         bounds = (0, cfg.img_tokens, cfg.tokens)
         chunks = tp.overlap_chunks
+
+        def run(s, r):
+            self.run_linear(lins[s], inp[r], gate=gates[s], residual=x[r] if first else None, out=x[r],
+                            bias=biases[s] if first else None)
+
         if chunks <= 1:
             for s in range(2):
-                r = slice(bounds[s], bounds[s + 1])
-                self.run_linear(lins[s], inp[r], gate=gates[s], residual=x[r] if last else None, out=x[r])
+                run(s, slice(bounds[s], bounds[s + 1]))
             tp.all_reduce(x)
             return
         # Chunk edges on 192-token tiles of the joint token range.
@@ -389,8 +565,7 @@ class DitStack:
                 for s in range(2):
                     lo, hi = max(a, bounds[s]), min(b, bounds[s + 1])
                     if lo < hi:
-                        r = slice(lo, hi)
-                        self.run_linear(lins[s], inp[r], gate=gates[s], residual=x[r] if last else None, out=x[r])
+                        run(s, slice(lo, hi))
                 works.append(tp.all_reduce_async(x[a:b]))
             for wk in works:
                 wk.wait()
@@ -421,6 +596,31 @@ def _modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, out: to
     n = F.layer_norm(x.float(), (x.shape[-1],), eps=1e-6)
     out.copy_(torch.addcmul(shift.float(), n, scale.float() + 1))
     return out
+
+
+def _residual_modulate(x: torch.Tensor, delta: torch.Tensor, bias: Optional[torch.Tensor],
+                       gate: Optional[torch.Tensor], shift: Optional[torch.Tensor], scale: Optional[torch.Tensor],
+                       out: Optional[torch.Tensor]) -> None:
+    """x = x + delta + gate * bias (one rounding), then, when `out` is given,
+    out = LayerNorm(x) * (1 + scale) + shift: one fused CUDA kernel
+    (qmm_residual_layernorm_modulate) on the GPU; torch ops on CPU tensors."""
+    if bias is None:
+        gate = None
+    if x.device.type == "cuda":
+        rows, hidden = x.shape
+        _lib.check(_lib.load().qmm_residual_layernorm_modulate(
+            x.data_ptr(), rows, hidden, delta.data_ptr(), None if bias is None else bias.data_ptr(),
+            None if gate is None else gate.data_ptr(), None if out is None else shift.data_ptr(),
+            None if out is None else scale.data_ptr(), 1e-6, None if out is None else out.data_ptr(),
+            _stream_handle(x.device)))
+        return
+    t = x.float() + delta.float()
+    if bias is not None:
+        t = t + (bias.float() * gate.float() if gate is not None else bias.float())
+    x.copy_(t.to(x.dtype))
+    if out is not None:
+        n = F.layer_norm(x.float(), (x.shape[-1],), eps=1e-6)
+        out.copy_(torch.addcmul(shift.float(), n, scale.float() + 1))
 
 
 def _sdpa(qkv: torch.Tensor, out: torch.Tensor, heads: int, head_dim: int) -> None:

@@ -34,6 +34,9 @@ from .weights import VarBuilder, WeightError
 ACTIVATIONS = {None: _lib.QMM_ACT_NONE, "none": _lib.QMM_ACT_NONE,
                "gelu_tanh": _lib.QMM_ACT_GELU_TANH, "silu": _lib.QMM_ACT_SILU}
 
+# Default of the epilogue-bias argument: the layer's own bias.
+OWN_BIAS = object()
+
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
@@ -102,13 +105,16 @@ class Affine:
     def run(self, x2d: torch.Tensor, *, gate: Optional[torch.Tensor] = None,
             residual: Optional[torch.Tensor] = None, activation: Optional[str] = None,
             out: Optional[torch.Tensor] = None, path: int = _lib.QMM_PATH_AUTO,
-            splits: Optional[int] = None) -> torch.Tensor:
+            splits: Optional[int] = None, bias=OWN_BIAS) -> torch.Tensor:
         """y [m, output] = residual + gate * act(x2d . W^T + bias).
 
         The GEMM (m > 16 under QMM_PATH_AUTO, or QMM_PATH_GEMM) splits K when
         the output tiles alone would leave most SMs idle; `splits` forces a
         split count (1 = none).  The f32 workspace comes from a per-device,
-        per-stream cache."""
+        per-stream cache.  `bias` replaces the layer's own bias in the
+        epilogue (None: no bias), e.g. for a row-parallel shard whose bias is
+        added once after the reduction."""
+        bias = self.bias if bias is OWN_BIAS else bias
         m = int(x2d.shape[0])
         n = self.output
         if out is None:
@@ -119,7 +125,9 @@ class Affine:
                 residual = residual.to(torch.bfloat16).contiguous()
         if gate is not None:
             gate = gate.reshape(n).to(torch.bfloat16).contiguous()
-        ep = QmmEpilogue(_ptr(self.bias), _ptr(gate), _ptr(residual), ACTIVATIONS[activation])
+        if bias is not None:
+            bias = bias.reshape(n).to(torch.bfloat16).contiguous()
+        ep = QmmEpilogue(_ptr(bias), _ptr(gate), _ptr(residual), ACTIVATIONS[activation])
         w = self.c_weight()
         lib = _lib.load()
         gemm = path == _lib.QMM_PATH_GEMM or (path == _lib.QMM_PATH_AUTO and m > 16)
@@ -132,21 +140,21 @@ class Affine:
                                                out.data_ptr(), sp, ws.data_ptr(), nbytes,
                                                _stream_handle(x2d.device))
                 if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
-                    return self._dense_fallback(x2d, gate, residual, activation, out)
+                    return self._dense_fallback(x2d, gate, residual, activation, out, bias)
                 _lib.check(status)
                 return out
         status = lib.qmm_linear_ex(ctypes.byref(w), x2d.data_ptr(), m, ctypes.byref(ep),
                                    out.data_ptr(), path, _stream_handle(x2d.device))
         if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
-            return self._dense_fallback(x2d, gate, residual, activation, out)
+            return self._dense_fallback(x2d, gate, residual, activation, out, bias)
         _lib.check(status)
         return out
 
-    def _dense_fallback(self, x2d, gate, residual, activation, out):
+    def _dense_fallback(self, x2d, gate, residual, activation, out, bias):
         # Dequantize on the GPU, dense GEMM, then the epilogue: the reference's
         # `self.dense()?.forward(x)` for layouts the fused kernel skips.
         t = torch.nn.functional.linear(x2d.float(), self.dequantize(torch.float32),
-                                       None if self.bias is None else self.bias.float())
+                                       None if bias is None else bias.float())
         if activation == "gelu_tanh":
             t = torch.nn.functional.gelu(t, approximate="tanh")
         elif activation == "silu":
@@ -230,10 +238,12 @@ class Linear:
     def forward_fused(self, x: torch.Tensor, *, gate: Optional[torch.Tensor] = None,
                       residual: Optional[torch.Tensor] = None,
                       activation: Optional[str] = None, path: int = _lib.QMM_PATH_AUTO,
-                      out: Optional[torch.Tensor] = None, splits: Optional[int] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, splits: Optional[int] = None,
+                      bias=OWN_BIAS) -> torch.Tensor:
         """residual + gate * act(x . W^T + bias) with any leading dims on x.
 
-        gate: [output] per-feature multiplier; residual: same shape as the output.
+        gate: [output] per-feature multiplier; residual: same shape as the output;
+        bias: replaces the layer's own bias (None: no bias).
         """
         if activation not in ACTIVATIONS:
             raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT, f"unknown activation {activation!r}")
@@ -263,7 +273,8 @@ class Linear:
             x2d = x2d.contiguous()
         if out is not None:
             out = out.view(m, a.output)
-        y = a.run(x2d, gate=gate, residual=residual, activation=activation, out=out, path=path, splits=splits)
+        y = a.run(x2d, gate=gate, residual=residual, activation=activation, out=out, path=path, splits=splits,
+                  bias=bias)
         return y.reshape(*lead, a.output)
 
 

@@ -8,7 +8,7 @@ weights and MLX's quantized_matmul output.  This script copies them, unchanged,
 into a numpy archive (bf16 as raw uint16 bits) so that the tests can run where
 the reference tree is absent.
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py <reference checkout>
 """
 import os
 import sys
@@ -19,7 +19,9 @@ from safetensors.torch import load_file
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <reference checkout (the directory holding tests/fixtures)>")
+    ref = sys.argv[1]
     src = os.path.join(ref, "tests", "fixtures", "quantized.safetensors")
     tensors = load_file(src)
     out = {}

@@ -81,13 +81,18 @@ def _bits32(t):
 _ACT_CODES = {None: 0, "none": 0, "gelu_tanh": 1, "silu": 2}
 
 
-def oracle_run_linear(lin, x, *, gate=None, residual=None, activation=None, out=None):
+_OWN = object()
+
+
+def oracle_run_linear(lin, x, *, gate=None, residual=None, activation=None, out=None, bias=_OWN):
     """The oracle's fused linear on CPU tensors, with the same signature as the
-    stack's CUDA linear: residual + gate * act(x . W^T + bias), rounded once."""
+    stack's CUDA linear: residual + gate * act(x . W^T + bias), rounded once
+    (`bias` other than the default replaces the layer's own; None: none)."""
     a = lin.affine
+    b = a.bias if bias is _OWN else bias
     m = x.numel() // a.input
     y = O.linear_f32(_bits16(x.reshape(m, a.input)), _bits32(a.packed), _bits16(a.scales),
-                     _bits16(a.offsets), a.bits, a.group, None if a.bias is None else _bits16(a.bias))
+                     _bits16(a.offsets), a.bits, a.group, None if b is None else _bits16(b.reshape(-1)))
     r = O.epilogue_bf16(y, None if gate is None else _bits16(gate.reshape(-1)),
                         None if residual is None else _bits16(residual.reshape(m, a.output)),
                         _ACT_CODES[activation])

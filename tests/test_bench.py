@@ -49,3 +49,44 @@ def test_reference_arm_prints_the_contract_line():
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in d["config"]
+
+
+def test_default_workload_is_the_tensor_parallel_stack():
+    old = sys.argv
+    try:
+        sys.argv = ["bench.py"]
+        a = bench.parse()
+    finally:
+        sys.argv = old
+    assert a.workload == "dit_2048_8bit" and a.gpus == 1 and a.steps == 10 and a.warmup == 3
+    assert not a.replicated
+
+
+def test_stack_layer_shapes_cover_every_linear_of_a_block():
+    from qwen_imager_b200.dit_stack import STACKS
+    cfg = STACKS["dit_2048_8bit"]
+    for world in (1, 2, 4, 8):
+        shapes = bench._layer_shapes(cfg, world)
+        flops = sum(2.0 * m * k * n * (2 if name == "modulation" else 1) for name, _s, m, k, n, _e in shapes)
+        # the block's linear FLOPs divided over the ranks
+        assert abs(flops * world - cfg.linear_flops_per_block()) < 1e-6 * flops * world, world
+
+
+def test_peak_choice_follows_the_timed_region():
+    burst, sustained, _, _ = bench.measured_peaks()
+    assert bench.choose_peak(0.02, {"reasons": ["sw_power_cap"], "sm_mhz": 1900, "sm_max_mhz": 1965})[0] == burst
+    assert bench.choose_peak(5.0, {"reasons": [], "sm_mhz": 1965, "sm_max_mhz": 1965})[0] == burst
+    assert bench.choose_peak(5.0, {"reasons": ["sw_power_cap"], "sm_mhz": 1400, "sm_max_mhz": 1965})[0] == sustained
+
+
+def test_stack_reference_arm_times_every_piece_of_a_block():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
+                          "--warmup", "1", "--workload", "dit_1024_4bit"],
+                         capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["unit"] == "ms" and d["higher_is_better"] is False
+    assert d["steps"] == 2 and d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"]
+    for piece in bench.STACK_PIECES:
+        assert piece in d["cpu_baseline"]["sample"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0
