@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define QMM_ABI_VERSION 1
+#define QMM_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define QMM_API __attribute__((visibility("default")))
@@ -80,8 +80,17 @@ typedef enum qmm_activation {
 } qmm_activation;
 
 /*
+ * Flag ORed into qmm_epilogue.activation: the residual operand multiplies
+ * instead of adding, y = residual * (gate * act(acc + bias)).  With the
+ * SiLU-activated gate projection of a SwiGLU MLP as the residual, the up
+ * projection's epilogue forms silu(x Wg^T) * (x Wu^T) (src/ops.rs:196-207).
+ */
+#define QMM_EPILOGUE_RESIDUAL_MUL 0x100
+
+/*
  * Fused epilogue, evaluated in f32 on the accumulator before one rounding to
- * bf16:  y = residual + gate * act(acc + bias).
+ * bf16:  y = residual + gate * act(acc + bias)  (or residual * (...), see
+ * QMM_EPILOGUE_RESIDUAL_MUL).
  * Every pointer may be NULL (term omitted).  bias and gate are bf16 [n]
  * (quant.rs:157-160 adds `bias`; src/dit.rs:88-93 multiplies by a per-feature
  * gate and adds the residual stream); residual is bf16 [m, n] and may alias y.
@@ -90,7 +99,7 @@ typedef struct qmm_epilogue {
     const uint16_t *bias;
     const uint16_t *gate;
     const uint16_t *residual;
-    int32_t activation;     /* qmm_activation */
+    int32_t activation;     /* qmm_activation, optionally | QMM_EPILOGUE_RESIDUAL_MUL */
 } qmm_epilogue;
 
 /* Kernel selection for qmm_linear_ex (tests and benchmarks). */
@@ -234,6 +243,18 @@ QMM_API uint64_t qmm_static_scratch_bytes(void);
  * counterpart in quant.rs (Metal has no bounded waits to report).
  */
 QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
+
+/*
+ * Test support for the bounded waits (no counterpart in quant.rs): for GEMM
+ * launches made after the call, in this process, every CTA's copy producer
+ * stops before its `withhold_block`-th k-block (-1: never), and every wait in
+ * the GEMM gives up after `wait_limit_ns` (1 ms .. 4 s; 0: the default 4 s).
+ * The waits for the withheld block then run out: the launch ends early with
+ * its output incomplete, having drained its own copies and MMAs and freed
+ * its tensor memory, and qmm_device_error reports QMM_ERR_TIMEOUT.  Call
+ * qmm_debug_gemm_stall(-1, 0) to restore normal launches.
+ */
+QMM_API qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns);
 
 /*
  * Caps the persistent kernels' grids at `sms` CTAs (0 = every SM) for launches

@@ -44,6 +44,8 @@ QMM_PATH_GEMV = 1
 QMM_PATH_GEMM = 2
 QMM_PATH_GEMM_PAIR = 3
 
+QMM_EPILOGUE_RESIDUAL_MUL = 0x100
+
 # Every symbol include/qmm.h declares.
 EXPORTED_SYMBOLS = (
     "qmm_abi_version",
@@ -64,6 +66,7 @@ EXPORTED_SYMBOLS = (
     "qmm_set_sm_budget",
     "qmm_static_scratch_bytes",
     "qmm_binary_version",
+    "qmm_debug_gemm_stall",
 )
 
 
@@ -155,6 +158,8 @@ def load() -> ctypes.CDLL:
         lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
         lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64
         lib.qmm_static_scratch_bytes.argtypes = []
+        lib.qmm_debug_gemm_stall.restype = i32
+        lib.qmm_debug_gemm_stall.argtypes = [i32, ctypes.c_uint64]
         lib.qmm_binary_version.restype = i32
         lib.qmm_binary_version.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32)]
         lib.qmm_device_error.restype = i32

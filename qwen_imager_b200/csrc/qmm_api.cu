@@ -14,6 +14,7 @@
 #include <mutex>
 #include <string>
 
+#include "qmm_common.cuh"
 #include "qmm_internal.h"
 
 namespace qmm {
@@ -77,6 +78,17 @@ int sm_count() {
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+namespace {
+std::atomic<int32_t> g_stall_block{-1};
+std::atomic<uint64_t> g_stall_wait_ns{0};
+}  // namespace
+
+void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns) {
+    *withhold = g_stall_block.load(std::memory_order_relaxed);
+    const uint64_t w = g_stall_wait_ns.load(std::memory_order_relaxed);
+    *wait_ns = w ? w : kWaitLimitNs;
+}
+
 bool gemv_pdl_enabled() {
     static const bool on = [] {
         const char *v = getenv("QMM_GEMV_PDL");
@@ -94,6 +106,12 @@ using qmm::fail;
 __global__ void qmm_arch_probe_kernel() {}
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// qmm_activation in the low byte, optionally QMM_EPILOGUE_RESIDUAL_MUL.
+static bool valid_activation(int32_t a) {
+    const int32_t act = a & 0xFF;
+    return (a & ~(0xFF | QMM_EPILOGUE_RESIDUAL_MUL)) == 0 && act >= QMM_ACT_NONE && act <= QMM_ACT_SILU;
+}
 
 static qmm_status check_device() {
     int dev = -1;
@@ -120,6 +138,16 @@ qmm_status qmm_binary_version(int32_t *binary_version, int32_t *ptx_version) {
     if (e != cudaSuccess) return qmm::cuda_fail(e, "kernel attributes");
     *binary_version = attr.binaryVersion;
     *ptx_version = attr.ptxVersion;
+    return QMM_OK;
+}
+
+qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns) {
+    if (withhold_block < -1) return fail(QMM_ERR_INVALID_ARGUMENT, "withheld block %d", withhold_block);
+    if (wait_limit_ns != 0 && (wait_limit_ns < 1000000ull || wait_limit_ns > qmm::kWaitLimitNs))
+        return fail(QMM_ERR_INVALID_ARGUMENT, "wait limit %llu ns is outside [1 ms, 4 s]",
+                    (unsigned long long)wait_limit_ns);
+    qmm::g_stall_block.store(withhold_block, std::memory_order_relaxed);
+    qmm::g_stall_wait_ns.store(wait_limit_ns, std::memory_order_relaxed);
     return QMM_OK;
 }
 
@@ -188,7 +216,7 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
     if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM_PAIR)
         return fail(QMM_ERR_INVALID_ARGUMENT, "unknown path %d", path);
     qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
-    if (e.activation < QMM_ACT_NONE || e.activation > QMM_ACT_SILU)
+    if (!valid_activation(e.activation))
         return fail(QMM_ERR_INVALID_ARGUMENT, "unknown activation %d", e.activation);
     if (!aligned16(x) || !aligned16(y) || (e.residual && !aligned16(e.residual)))
         return fail(QMM_ERR_MISALIGNED, "x, y and residual must be 16-byte aligned");
@@ -241,7 +269,7 @@ qmm_status qmm_linear_splitk(const qmm_weight *w, const uint16_t *x, int64_t m, 
     if (!x || !y) return fail(QMM_ERR_INVALID_ARGUMENT, "null x or y");
     if (splits < 1 || splits > 16) return fail(QMM_ERR_INVALID_ARGUMENT, "split count %d is not in [1, 16]", splits);
     qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
-    if (e.activation < QMM_ACT_NONE || e.activation > QMM_ACT_SILU)
+    if (!valid_activation(e.activation))
         return fail(QMM_ERR_INVALID_ARGUMENT, "unknown activation %d", e.activation);
     if (!aligned16(x) || !aligned16(y) || (e.residual && !aligned16(e.residual)))
         return fail(QMM_ERR_MISALIGNED, "x, y and residual must be 16-byte aligned");

@@ -127,10 +127,10 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t pa
 
 // Waits for the phase of `bar` with parity `parity` to complete.  Returns
 // false (and records `code` in *err unless another error is already there)
-// when the wait exceeds kWaitLimitNs or when another role already failed.
+// when the wait exceeds `limit_ns` or when another role already failed.
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
-                                          uint32_t code) {
+                                          uint32_t code, uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t addr = smem_u32(bar);
     auto try_once = [&]() {
         return CLUSTER ? mbar_try_wait_cluster(addr, parity) : mbar_try_wait(addr, parity);
@@ -149,7 +149,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
         if (ns < 128) ns <<= 1;
         if ((it & 15) == 0) {
             if (*reinterpret_cast<volatile uint32_t *>(err) != kErrNone) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 atomicCAS(err, kErrNone, code);
                 return false;
             }

@@ -1,4 +1,7 @@
-// Fused epilogue: y = residual + gate * act(acc + bias), f32, one bf16 rounding.
+// Fused epilogue: y = residual + gate * act(acc + bias), f32, one bf16 rounding;
+// with kEpiResidualMul in the activation field the residual operand multiplies
+// instead: y = residual * (gate * act(acc + bias)) (the up projection of a
+// SwiGLU MLP times the SiLU-activated gate projection, src/ops.rs:203).
 // The reference applies these as separate bf16 tensor ops after the linear
 // (image-forger src/quant.rs:157-160 bias; src/dit.rs:88-93 gate and residual).
 #pragma once
@@ -7,7 +10,12 @@
 
 namespace qmm {
 
+// Bit of EpilogueArgs::act (QMM_EPILOGUE_RESIDUAL_MUL): the residual multiplies.
+constexpr int32_t kEpiResidualMul = 0x100;
+constexpr int32_t kEpiActMask = 0xFF;
+
 __device__ __forceinline__ float apply_activation(float t, int act) {
+    act &= kEpiActMask;
     if (act == 1) {  // GELU, tanh approximation
         const float c = 0.7978845608028654f;
         return 0.5f * t * (1.0f + tanhf(c * (t + 0.044715f * t * t * t)));
@@ -43,7 +51,10 @@ __device__ __forceinline__ float epilogue_value(const EpilogueArgs &e, const Fea
                                                 float acc, const uint16_t *residual_elem) {
     float t = apply_activation(acc + c.bias, e.act);
     if (e.gate) t = t * c.gate;
-    if (residual_elem) t = bf16_bits_to_f32(*residual_elem) + t;
+    if (residual_elem) {
+        const float r = bf16_bits_to_f32(*residual_elem);
+        t = (e.act & kEpiResidualMul) ? r * t : r + t;
+    }
     return t;
 }
 
@@ -53,7 +64,7 @@ __device__ __forceinline__ float epilogue_value_rv(const EpilogueArgs &e, const 
                                                    float acc, float resid) {
     float t = apply_activation(acc + c.bias, e.act);
     if (e.gate) t = t * c.gate;
-    if (e.residual) t = resid + t;
+    if (e.residual) t = (e.act & kEpiResidualMul) ? resid * t : resid + t;
     return t;
 }
 

@@ -111,6 +111,12 @@ struct Params {
     // buffer (needs a residual, no split-K and n % 8 == 0).
     int32_t res_tma;
     uint32_t *err;
+    // Limit of every bounded wait (kWaitLimitNs unless a test shortens it).
+    uint64_t wait_ns;
+    // Test support (qmm_debug_gemm_stall): the producer of every CTA stops
+    // before its `withhold`-th k-block (-1: never), so that the waits for
+    // that block run out and the error path runs.
+    int32_t withhold;
 };
 
 // Byte offset of 16-byte chunk `c` of row `r` in a TMA tile written with
@@ -257,7 +263,11 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
             const int m0 = (tile / p.w_tiles) * T + (int)rank * C::kXRows;
             for (int kb = kb0; kb < kb0 + nkb; ++kb, ++i) {
-                if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer)) {
+                if ((int32_t)i == p.withhold) {  // test support: this block's copies are never issued
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer, p.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             // Let the copies already issued land before the CTA exits.
             const uint32_t first = i > (uint32_t)S ? i - S : 0;
             for (uint32_t j = first; j < i; ++j)
-                mbar_wait<PAIR>(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain);
+                mbar_wait<PAIR>(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain, p.wait_ns);
         }
     } else if (warp == W::kMma) {
         // ---------------------------------------------------------- MMA issuer
@@ -303,7 +313,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             int lt = 0;
             for (int wu = unit; ok && wu < p.num_units; wu += nunits, ++lt) {
                 const int b = lt & 1;
-                ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma));
+                ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma, p.wait_ns));
                 if (!ok) break;
                 tc_fence_after_sync();
                 const uint32_t d = tmem + C::kAcc0 + b * T;
@@ -313,7 +323,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     // afull implies full[s] and full[s + 1] as below.
                     for (int kb = 0; kb < nkb; kb += 2) {
                         const int pb = a >> 1;
-                        ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[pb], ph_a, p.err, kErrTimeoutMma));
+                        ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[pb], ph_a, p.err, kErrTimeoutMma, p.wait_ns));
                         if (!ok) break;
                         tc_fence_after_sync();
                         const int s1 = s + 1 == S ? 0 : s + 1;
@@ -354,9 +364,9 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     // complete, so the release/acquire chain through afull[a]
                     // orders the MMA's shared-memory reads after those copies.
                     // A CTA pair also needs the peer's x tile: xfull[s].
-                    ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma) &&
+                    ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma, p.wait_ns) &&
                                                      (!PAIR || mbar_wait<PAIR>(&xfull[s], ph_s, p.err,
-                                                                               kErrTimeoutMma)));
+                                                                               kErrTimeoutMma, p.wait_ns)));
                     if (!ok) break;
                     tc_fence_after_sync();
                     const uint32_t atm = tmem + C::kASlot0 + a * 32;
@@ -402,7 +412,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     else tc_commit(drain);
                 }
                 __syncwarp();
-                mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain);
+                mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain, p.wait_ns);
             }
         }
     } else if (warp >= W::kDq0) {
@@ -461,7 +471,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             if (i + SETS < total_blocks) load_meta(nkb_i, n0m, n1m);
             // The codes are dequantized as soon as they land; only the store
             // into the TMEM A slot waits for the MMA that last read the slot.
-            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant)) break;
+            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant, p.wait_ns)) break;
             const uint8_t *pst = smem + C::kPOff + s * C::kPStageBytes;
             constexpr int kV = HALVES == 1 ? 32 : 16;
             uint32_t v[kV];
@@ -470,7 +480,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
             const int ab = p.kpair ? (a >> 1) : a;  // the slot's barrier (shared by a slot pair)
-            if (!mbar_wait<PAIR>(&aempty[ab], ph_a ^ 1, p.err, kErrTimeoutDequant)) break;
+            if (!mbar_wait<PAIR>(&aempty[ab], ph_a ^ 1, p.err, kErrTimeoutDequant, p.wait_ns)) break;
             if constexpr (HALVES == 1) tmem_st_32x32b_x32(tcol + a * 32, v);
             else tmem_st_32x32b_x16(tcol + a * 32, v);
             tc_wait_st();
@@ -520,7 +530,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             const int m0 = (tile / p.w_tiles) * T;
             // The four epilogue warps leave together (they meet at named
             // barriers below): one expired wait ends the loop for all.
-            const bool waited = mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue);
+            const bool waited = mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue, p.wait_ns);
             if (named_barrier_or(1, kEpiWarps * 32, !waited)) break;
             tc_fence_after_sync();
             const int64_t n = n0 + quad * 32 + lane;
@@ -571,7 +581,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     if (p.res_tma) {
                         // This chunk's residual is in the staging buffer: read
                         // it and overwrite it with the output in place.
-                        mbar_wait<PAIR>(&rfull[eb], (chunk >> 1) & 1, p.err, kErrTimeoutEpilogue);
+                        mbar_wait<PAIR>(&rfull[eb], (chunk >> 1) & 1, p.err, kErrTimeoutEpilogue, p.wait_ns);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             uint16_t &slot = st16[j * kWRows + quad * 32 + lane];
@@ -631,7 +641,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         }
         if (quad == 0 && lane == 0) {
             // On an early exit a prefetched residual chunk may still be landing.
-            if (res_pending) mbar_wait<PAIR>(&rfull[chunk & 1], (chunk >> 1) & 1, p.err, kErrTimeoutDrain);
+            if (res_pending) mbar_wait<PAIR>(&rfull[chunk & 1], (chunk >> 1) & 1, p.err, kErrTimeoutDrain, p.wait_ns);
             bulk_wait_all();  // the stores have landed before the CTA exits
         }
     }
@@ -802,6 +812,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.kpair = (!PAIR && SETS == 4 && HALVES == 1 && C::kASlots == 4 && p.kbs % 2 == 0) ? 1 : 0;
     p.res_tma = res_tma ? 1 : 0;
     p.err = device_error_word();
+    debug_gemm_stall(&p.withhold, &p.wait_ns);
     const int ctas = PAIR ? 2 : 1;
     const int units = (int)std::min<int64_t>(p.num_units, sm_count() / ctas);
     cudaLaunchConfig_t cfg = {};

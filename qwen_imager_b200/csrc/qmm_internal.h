@@ -27,6 +27,10 @@ void count_launch(uint64_t n = 1);
 // previous kernel of its stream (on unless QMM_GEMV_PDL=0; read once).
 bool gemv_pdl_enabled();
 
+// Test support: the GEMM's withheld k-block (-1: none) and wait limit for the
+// next launches (qmm_debug_gemm_stall).
+void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns);
+
 // Launchers.  Arguments are validated by the caller (qmm_api.cu).
 qmm_status launch_dequantize(const qmm_weight &w, void *dst, int32_t dtype, cudaStream_t st);
 

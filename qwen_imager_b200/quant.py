@@ -105,8 +105,9 @@ class Affine:
     def run(self, x2d: torch.Tensor, *, gate: Optional[torch.Tensor] = None,
             residual: Optional[torch.Tensor] = None, activation: Optional[str] = None,
             out: Optional[torch.Tensor] = None, path: int = _lib.QMM_PATH_AUTO,
-            splits: Optional[int] = None, bias=OWN_BIAS) -> torch.Tensor:
-        """y [m, output] = residual + gate * act(x2d . W^T + bias).
+            splits: Optional[int] = None, bias=OWN_BIAS, residual_mul: bool = False) -> torch.Tensor:
+        """y [m, output] = residual + gate * act(x2d . W^T + bias)
+        (residual * (...) with residual_mul).
 
         The GEMM (m > 16 under QMM_PATH_AUTO, or QMM_PATH_GEMM) splits K when
         the output tiles alone would leave most SMs idle; `splits` forces a
@@ -127,7 +128,8 @@ class Affine:
             gate = gate.reshape(n).to(torch.bfloat16).contiguous()
         if bias is not None:
             bias = bias.reshape(n).to(torch.bfloat16).contiguous()
-        ep = QmmEpilogue(_ptr(bias), _ptr(gate), _ptr(residual), ACTIVATIONS[activation])
+        act_code = ACTIVATIONS[activation] | (_lib.QMM_EPILOGUE_RESIDUAL_MUL if residual_mul else 0)
+        ep = QmmEpilogue(_ptr(bias), _ptr(gate), _ptr(residual), act_code)
         w = self.c_weight()
         lib = _lib.load()
         gemm = path == _lib.QMM_PATH_GEMM or (path == _lib.QMM_PATH_AUTO and m > 16)
@@ -140,17 +142,17 @@ class Affine:
                                                out.data_ptr(), sp, ws.data_ptr(), nbytes,
                                                _stream_handle(x2d.device))
                 if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
-                    return self._dense_fallback(x2d, gate, residual, activation, out, bias)
+                    return self._dense_fallback(x2d, gate, residual, activation, out, bias, residual_mul)
                 _lib.check(status)
                 return out
         status = lib.qmm_linear_ex(ctypes.byref(w), x2d.data_ptr(), m, ctypes.byref(ep),
                                    out.data_ptr(), path, _stream_handle(x2d.device))
         if status == _lib.QMM_ERR_UNSUPPORTED and path == _lib.QMM_PATH_AUTO:
-            return self._dense_fallback(x2d, gate, residual, activation, out, bias)
+            return self._dense_fallback(x2d, gate, residual, activation, out, bias, residual_mul)
         _lib.check(status)
         return out
 
-    def _dense_fallback(self, x2d, gate, residual, activation, out, bias):
+    def _dense_fallback(self, x2d, gate, residual, activation, out, bias, residual_mul=False):
         # Dequantize on the GPU, dense GEMM, then the epilogue: the reference's
         # `self.dense()?.forward(x)` for layouts the fused kernel skips.
         t = torch.nn.functional.linear(x2d.float(), self.dequantize(torch.float32),
@@ -162,8 +164,8 @@ class Affine:
         if gate is not None:
             t = t * gate.float()
         if residual is not None:
-            t = residual.float() + t
-        out.copy_(t.to(torch.bfloat16))
+            t = residual.float() * t if residual_mul else residual.float() + t
+        out.copy_(t.to(out.dtype))
         return out
 
 
@@ -201,8 +203,8 @@ class Linear:
                               f"or 8-bit for {input} inputs") from exc
         return cls(affine=Affine(
             packed=packed,
-            scales=scales,
-            offsets=vb.get((output, groups), "biases"),
+            scales=_as_bf16(scales, vb, "scales"),
+            offsets=_as_bf16(vb.get((output, groups), "biases"), vb, "biases"),
             bias=vb.get(output, "bias") if bias else None,
             bits=bits,
             group=group,
@@ -239,43 +241,77 @@ class Linear:
                       residual: Optional[torch.Tensor] = None,
                       activation: Optional[str] = None, path: int = _lib.QMM_PATH_AUTO,
                       out: Optional[torch.Tensor] = None, splits: Optional[int] = None,
-                      bias=OWN_BIAS) -> torch.Tensor:
+                      bias=OWN_BIAS, residual_mul: bool = False) -> torch.Tensor:
         """residual + gate * act(x . W^T + bias) with any leading dims on x.
 
         gate: [output] per-feature multiplier; residual: same shape as the output;
-        bias: replaces the layer's own bias (None: no bias).
+        bias: replaces the layer's own bias (None: no bias); residual_mul: the
+        residual multiplies instead, residual * (gate * act(x . W^T + bias)).
+
+        bf16 inputs run the fused kernels.  f32 inputs take the reference's
+        non-fused route (src/quant.rs:121): the weight dequantized to f32
+        (bit-exact) and a dense f32 GEMM, with an f32 result.
         """
         if activation not in ACTIVATIONS:
             raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT, f"unknown activation {activation!r}")
         *lead, k = x.shape
         if self.affine is None:
             _require_cuda(x, "input")
-            t = torch.nn.functional.linear(x, self._weight, self._bias)
-            if activation == "gelu_tanh":
-                t = torch.nn.functional.gelu(t, approximate="tanh")
-            elif activation == "silu":
-                t = torch.nn.functional.silu(t)
-            if gate is not None:
-                t = t * gate
-            if residual is not None:
-                t = residual + t
-            return t
+            t = torch.nn.functional.linear(x, self._weight, self._bias if bias is OWN_BIAS else bias)
+            return _epilogue_torch(t, gate, residual, activation, residual_mul)
         a = self.affine
         if k != a.input:
             raise QmmError(_lib.QMM_ERR_BAD_SHAPE, f"quantized linear expects {a.input} inputs, got {k}")
         _require_cuda(x, "input")
+        m = x.numel() // k if k else 0
+        if x.dtype == torch.float32:
+            b = a.bias if bias is OWN_BIAS else bias
+            t = torch.nn.functional.linear(x.reshape(m, k), a.dequantize(torch.float32),
+                                           None if b is None else b.float())
+            t = _epilogue_torch(t, gate, None if residual is None else residual.reshape(m, a.output),
+                                activation, residual_mul)
+            if out is not None:
+                out.view(m, a.output).copy_(t)
+                return out
+            return t.reshape(*lead, a.output)
         if x.dtype != torch.bfloat16:
             raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT,
-                           f"quantized linear computes in bf16; got {x.dtype} input")
-        m = x.numel() // k if k else 0
+                           f"quantized linear computes in bf16 (or f32 through dequantization); got {x.dtype}")
         x2d = x.reshape(m, k)
         if not x2d.is_contiguous() or x2d.data_ptr() % 16:
             x2d = x2d.contiguous()
         if out is not None:
             out = out.view(m, a.output)
         y = a.run(x2d, gate=gate, residual=residual, activation=activation, out=out, path=path, splits=splits,
-                  bias=bias)
+                  bias=bias, residual_mul=residual_mul)
         return y.reshape(*lead, a.output)
+
+
+def _epilogue_torch(t, gate, residual, activation, residual_mul):
+    """The fused epilogue's arithmetic with torch ops, in t's dtype."""
+    if activation == "gelu_tanh":
+        t = torch.nn.functional.gelu(t, approximate="tanh")
+    elif activation == "silu":
+        t = torch.nn.functional.silu(t)
+    if gate is not None:
+        t = t * gate.to(t.dtype)
+    if residual is not None:
+        r = residual.to(t.dtype)
+        t = r * t if residual_mul else r + t
+    return t
+
+
+def _as_bf16(t: torch.Tensor, vb: VarBuilder, name: str) -> torch.Tensor:
+    """Scales and offsets as the kernels read them (bf16).  MLX stores them in
+    bf16, so a builder in another float dtype (e.g. f32, as the reference's
+    f32 tests load them) converts back exactly; values that bf16 cannot hold
+    are an error rather than a silent rounding."""
+    if t.dtype == torch.bfloat16:
+        return t
+    b = t.to(torch.bfloat16)
+    if not torch.equal(b.to(t.dtype), t):
+        raise WeightError(f"{vb.prefix()}: {name} in {t.dtype} are not exact in bf16, which the kernels read")
+    return b
 
 
 def linear(vb: VarBuilder, input: int, output: int, bias: bool) -> Linear:

@@ -25,7 +25,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.qmm_abi_version() == 1
+    assert lib.qmm_abi_version() == 2
 
 
 @pytest.mark.gpu
