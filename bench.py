@@ -51,6 +51,11 @@ WORKLOADS = {
     "ffn_down": ("FFN down 4-bit [4352x12288]x[3072x12288]^T + fused residual, GELU-tanh input",
                  [(4352, 12288, 3072, 4, {"residual": True, "gelu_input": True})], 2),
     "adaln_gemv": ("adaLN GEMV 4-bit [1x3072]x[18432x3072]^T", [(1, 3072, 18432, 4, {"silu_input": True})], 1),
+    "adaln_gemv_8bit": ("adaLN GEMV 8-bit [1x3072]x[18432x3072]^T (the 2048x2048 stack's modulation)",
+                        [(1, 3072, 18432, 8, {"silu_input": True})], 5),
+    # The 2048x2048 stack's image-stream FFN-up GEMM on one rank (for profiles).
+    "stack_img_up": ("image-stream FFN up 8-bit [16384x3072]x[12288x3072]^T + GELU-tanh",
+                     [(16384, 3072, 12288, 8, {"activation": "gelu_tanh"})], 6),
 }
 STACK_WORKLOADS = {
     "dit_1024_4bit": "60-block dual-stream DiT linear stack, 1024x1024 (4096 image + 256 text tokens), 4-bit",
@@ -235,8 +240,11 @@ def run_ours(args, rank, world, device):
         for li, rot in enumerate(sets):
             if only is None or only == li:
                 lin, x, res, y = rot[i % len(rot)]
-                lin.forward_fused(x, residual=res, out=y)
+                lin.forward_fused(x, residual=res, out=y, activation=layers[li][4].get("activation"))
 
+    # Weights are written once, before the step: the streaming GEMV may fetch
+    # them before the kernel ahead of it completes.
+    _lib.load().qmm_set_weights_immutable(1)
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize()
@@ -315,12 +323,12 @@ def run_ours(args, rank, world, device):
         d2h = sum(hy.numel() * 2 for _, _, hy in host)
 
         def e2e_step(i):
-            for rot, (hx, hr, hy) in zip(sets, host):
+            for li, (rot, (hx, hr, hy)) in enumerate(zip(sets, host)):
                 lin, x, res, y = rot[i % len(rot)]
                 x.copy_(hx, non_blocking=True)
                 if hr is not None:
                     res.copy_(hr, non_blocking=True)
-                lin.forward_fused(x, residual=res, out=y)
+                lin.forward_fused(x, residual=res, out=y, activation=layers[li][4].get("activation"))
                 hy.copy_(y, non_blocking=True)
 
         for i in range(2):
@@ -818,7 +826,9 @@ def main():
               "parallelism": f"dp{world} (independent token batches)",
               "l2": "per linear " + "/".join(str(rotation(l)) for l in layers)
                     + " rotating weight/input sets, together at least 2x the 126 MB L2 (no flush)",
-              "launch": "the K timed steps replayed as one CUDA graph; e2e through the eager public API"}
+              "launch": "the K timed steps replayed as one CUDA graph; e2e through the eager public API",
+              "weights": "immutable after load (qmm_set_weights_immutable(1): the GEMVs stream weights before "
+                         "their dependency wait)"}
 
     if args.impl == "reference":
         if rank != 0:

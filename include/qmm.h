@@ -257,6 +257,20 @@ QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
 QMM_API qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns);
 
 /*
+ * Declares (on != 0) that no kernel writes the packed codes, scales or offsets
+ * of the weights this process passes to the library while launches that use
+ * them may run: weights are loaded once and then only read, as the
+ * reference's immutable shared weight buffers (src/shared.rs:148-184).  The
+ * tensor-core GEMV then streams its weights without waiting for the kernel
+ * before it on the stream (programmatic dependent launch), so they arrive
+ * while that kernel drains; x, bias, gate and residual are still read, and y
+ * written, only after it has completed.  Off by default.  Applies to launches
+ * made after the call, in this process; returns the previous setting.  No
+ * counterpart in quant.rs.
+ */
+QMM_API int32_t qmm_set_weights_immutable(int32_t on);
+
+/*
  * Caps the persistent kernels' grids at `sms` CTAs (0 = every SM) for launches
  * made after the call, in this process; returns the previous cap.  Leaves SMs
  * free for kernels that run concurrently on other streams (e.g. a collective

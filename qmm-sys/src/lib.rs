@@ -106,6 +106,7 @@ extern "C" {
     pub fn qmm_static_scratch_bytes() -> u64;
     pub fn qmm_device_error(stream: *mut c_void, code_out: *mut u32) -> qmm_status;
     pub fn qmm_debug_gemm_stall(withhold_block: i32, wait_limit_ns: u64) -> qmm_status;
+    pub fn qmm_set_weights_immutable(on: i32) -> i32;
     pub fn qmm_set_sm_budget(sms: i32) -> i32;
     pub fn qmm_binary_version(binary_version: *mut i32, ptx_version: *mut i32) -> qmm_status;
     pub fn qmm_launch_count() -> u64;

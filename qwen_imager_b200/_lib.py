@@ -67,6 +67,7 @@ EXPORTED_SYMBOLS = (
     "qmm_static_scratch_bytes",
     "qmm_binary_version",
     "qmm_debug_gemm_stall",
+    "qmm_set_weights_immutable",
 )
 
 
@@ -158,6 +159,8 @@ def load() -> ctypes.CDLL:
         lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
         lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64
         lib.qmm_static_scratch_bytes.argtypes = []
+        lib.qmm_set_weights_immutable.restype = i32
+        lib.qmm_set_weights_immutable.argtypes = [i32]
         lib.qmm_debug_gemm_stall.restype = i32
         lib.qmm_debug_gemm_stall.argtypes = [i32, ctypes.c_uint64]
         lib.qmm_binary_version.restype = i32

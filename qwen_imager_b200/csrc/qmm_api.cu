@@ -89,6 +89,12 @@ void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns) {
     *wait_ns = w ? w : kWaitLimitNs;
 }
 
+namespace {
+std::atomic<int32_t> g_weights_immutable{0};
+}  // namespace
+
+bool weights_immutable() { return g_weights_immutable.load(std::memory_order_relaxed) != 0; }
+
 bool gemv_pdl_enabled() {
     static const bool on = [] {
         const char *v = getenv("QMM_GEMV_PDL");
@@ -149,6 +155,10 @@ qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns) 
     qmm::g_stall_block.store(withhold_block, std::memory_order_relaxed);
     qmm::g_stall_wait_ns.store(wait_limit_ns, std::memory_order_relaxed);
     return QMM_OK;
+}
+
+int32_t qmm_set_weights_immutable(int32_t on) {
+    return qmm::g_weights_immutable.exchange(on ? 1 : 0, std::memory_order_relaxed);
 }
 
 int32_t qmm_set_sm_budget(int32_t sms) {

@@ -291,6 +291,11 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                 }
             }
         }
+        // This CTA issues no more loads: a kernel launched after this one as a
+        // programmatic dependent (the streaming GEMV) may take SMs as the
+        // CTAs of this grid exit; it reads this grid's outputs only after
+        // its dependency wait.
+        pdl_launch_dependents();
         if (!ok) {
             // Let the copies already issued land before the CTA exits.
             const uint32_t first = i > (uint32_t)S ? i - S : 0;

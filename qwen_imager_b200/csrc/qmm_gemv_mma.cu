@@ -32,6 +32,18 @@
 // reads (g = 0..3 or 4..7) sit in different quads, whose slots start 32 bytes
 // apart modulo 128, so they hit disjoint banks.
 //
+// 8-bit codes.  An 8-bit code q = lo + 16 hi is two consecutive nibbles of
+// the packed word, so an 8-bit row of K codes is a row of 2K nibbles and runs
+// through the same MMAs: x is staged as the pair (x_j, 16 x_j) for the
+// nibbles (lo_j, hi_j) (exact in bf16), so that D_u = sum x'(128 + nibble)
+// and sum_j x_j q_j = D_u - 128 * 17 * X_u; per unit of 32 codes (64 nibbles)
+//   sum_j x_j (s q_j + o) = s * D_u + (o - 2176 s) * X_u.
+//
+// Weights immutable (qmm_set_weights_immutable): the producer streams the
+// first ring stages of codes, scales and offsets without waiting for the
+// previous kernel, so they arrive while that kernel drains; x and the
+// epilogue inputs are still read only after the dependency wait.
+//
 // Launch.  With programmatic dependent launch the next launch's CTAs take
 // each SM as soon as this grid's CTA there exits, instead of after the whole
 // grid drains and a new launch ramps up.  Every read of codes, scales, x,
@@ -76,6 +88,7 @@ struct Params {
     int32_t row_bytes, quad_stride, nblocks;   // quad slot = 4 rows + 32 bytes
     int32_t stage_bytes, meta_off;            // scales at meta_off, offsets after them
     int32_t xp_stride;                        // u32 words per staged token
+    int32_t prefetch_weights;                 // codes/scales/offsets streamed before the dependency wait
     uint32_t *err;
 };
 
@@ -140,14 +153,65 @@ __device__ __forceinline__ void stage_x(const uint16_t *x, uint32_t *xp, float *
     }
 }
 
+// 8-bit codes as nibble pairs: unit u of the nibble row covers codes
+// [32u, 32u + 32); nibble c of the unit is code 32u + c/2, with x weighted by
+// 16 for odd c (the high nibble).  Entry (token, u, t, j, r) holds x' at
+// nibbles c0 = 16t + 8(j/2) + (j%2) + 4r and c0 + 2, as in stage_x; one task
+// per (token, u, t) reads its 8 codes with one 16-byte load.  X_u is the sum
+// of the 32 codes' x (not x').
+template <int MP>
+__device__ __forceinline__ void stage_x8(const uint16_t *x, uint32_t *xp, float *xsum, int m, int k, int units,
+                                         int xp_stride, int tid, int nthreads) {
+    for (int i = tid; i < units * 32; i += nthreads) xp[(size_t)m * xp_stride + i] = 0u;
+    for (int i = tid; i < units * MP; i += nthreads)
+        if (i % MP >= m) xsum[i] = 0.0f;
+    const int tasks = m * units * 4;
+    const int tasks_rounded = (tasks + 31) & ~31;
+    for (int base = 0; base < tasks_rounded; base += nthreads) {
+        const int i = base + tid;
+        const bool act = i < tasks;
+        const int t = i & 3, ut = i >> 2;
+        const int tok = act ? ut / units : 0, u = act ? ut - tok * units : 0;
+        float sum = 0.0f;
+        if (act) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x + (size_t)tok * k + u * (kUnit / 2) + 8 * t));
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};  // codes 2i | 2i+1
+            auto xnib = [&](int c) -> uint32_t {  // x' of nibble c of this task (bf16 bits)
+                const int code = c >> 1;
+                const uint32_t b = (w[code >> 1] >> ((code & 1) * 16)) & 0xFFFFu;
+                if (!(c & 1)) return b;
+                const __nv_bfloat16 h = __float2bfloat16_rn(bf16_bits_to_f32(b) * 16.0f);  // exact
+                return *reinterpret_cast<const uint16_t *>(&h);
+            };
+            uint32_t out[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int jj = e >> 1, r = e & 1;
+                const int c0 = 8 * (jj >> 1) + (jj & 1) + 4 * r;
+                out[e] = xnib(c0) | (xnib(c0 + 2) << 16);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)tok * xp_stride + u * 32 + t * 8);
+            dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+            dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (act && t == 0) xsum[u * MP + tok] = sum;
+    }
+}
+
 // Shared memory (16-byte aligned regions):
 //   stages [stages][rb / 4 quad slots of codes | rb*groups scales | rb*groups offsets]
 //   xp     [m + 1][units][4 lanes t][4 MMAs j][2] u32   x in MMA order (bf16 pairs); row m zero
 //   xsum   [units][MP] f32                            X_u per token (zero beyond m)
 //   part   [2][ks][rb][m] f32                         partial sums per K slice (ks = 16 warps)
 //   bars   full[kMaxStages], empty[kMaxStages], pready[2], pfree[2]
-template <int MT, int TPW, int CW>
+template <int BITS, int MT, int TPW, int CW>
 __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(const Params p) {
+    // sum_j x_j q_j = D_u - kOff * X_u (see the header comment).
+    constexpr float kOff = BITS == 4 ? 128.0f : 2176.0f;
     using W = Warps<CW>;
     constexpr int MP = 8 * MT;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -207,7 +271,8 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 
     if (warp == W::kProducer) {
         // ---------------------------------------------------------- producer
-        pdl_dependency_wait();
+        // Weights that no kernel writes need not wait for the previous one.
+        if (!p.prefetch_weights) pdl_dependency_wait();
         int j = 0;
         for (int b = blockIdx.x; b < p.nblocks; b += gridDim.x, ++j) {
             const int s = j % p.stages;
@@ -234,7 +299,8 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
     // ------------------------------------------------- stage x in MMA order
     const int consumer_threads = CW * 32;
     pdl_dependency_wait();  // x may come from the previous kernel
-    stage_x<MP>(p.x, xp, xsum, p.m, p.k, p.units, p.xp_stride, threadIdx.x, consumer_threads);
+    if constexpr (BITS == 4) stage_x<MP>(p.x, xp, xsum, p.m, p.k, p.units, p.xp_stride, threadIdx.x, consumer_threads);
+    else stage_x8<MP>(p.x, xp, xsum, p.m, p.k, p.units, p.xp_stride, threadIdx.x, consumer_threads);
     named_barrier(1, consumer_threads);
 
     // ---------------------------------------------------------- consumers
@@ -314,7 +380,7 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
                     for (int hr = 0; hr < 2; ++hr) {
                         const int row = (tile0 + tl) * 16 + 4 * (g & 3) + (g >> 2) + 2 * hr;  // block row
                         const float sv = bf16_bits_to_f32(ssc[row * p.groups + gi]);
-                        const float cv = fmaf(-128.0f, sv, bf16_bits_to_f32(sof[row * p.groups + gi]));
+                        const float cv = fmaf(-kOff, sv, bf16_bits_to_f32(sof[row * p.groups + gi]));
                         sc[tl][hr] = make_float2(sv, sv);
                         cc[tl][hr] = make_float2(cv, cv);
                     }
@@ -364,16 +430,22 @@ struct Plan {
     size_t smem;
 };
 
+// Units are 64 nibbles: 64 codes at 4 bits, 32 codes at 8 bits.
+static int64_t units_of(const qmm_weight &w) { return w.k * w.bits / 4 / kUnit; }
+
 static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     pl.cw = 16;
     const int mt = m <= 8 ? 1 : 2;
-    const int64_t units = w.k / kUnit, groups = w.k / w.group;
-    const int64_t row_bytes = w.k / 2;
+    const int64_t units = units_of(w), groups = w.k / w.group;
+    const int64_t row_bytes = w.k * w.bits / 8;
     // 4 * row_bytes is a multiple of 128 (k % 64 == 0): quad slots 32 bytes
     // longer start 0, 32, 64, 96 bytes modulo 128 apart.
     pl.quad_stride = (int)(4 * row_bytes + 32);
     pl.xp_stride = (int)(units * 32 + 4);  // +16 bytes: tokens start in different bank quads
     const size_t xs = (size_t)(m + 1) * pl.xp_stride * 4 + (size_t)units * 8 * mt * 4;
+    // A 32-row block (two tiles per warp) when three ring stages fit, else a
+    // 16-row block; with neither, any that fits two stages.
+    for (int pass = 0; pass < 2; ++pass)
     for (int rb = 32; rb >= 16; rb /= 2) {
         // 16 warps on a 32-row block: one tile group of two tiles; otherwise
         // one tile per warp and rb / 16 tile groups.
@@ -384,7 +456,7 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
         const size_t fixed = xs + 2 * (size_t)ks * rb * m * 4 + 16 + (2 * kMaxStages + 4) * 8 + 64;
         int stages = kMaxStages;
         while (stages >= 2 && fixed + (size_t)stages * stage > kSmemLimit) --stages;
-        if (stages < 2) continue;
+        if (stages < (pass == 0 ? 3 : 2)) continue;
         pl.rb = rb;
         pl.ks = ks;
         pl.tpw = tpw;
@@ -397,7 +469,7 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     return false;
 }
 
-template <int MT, int TPW, int CW>
+template <int BITS, int MT, int TPW, int CW>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
                            uint16_t *y, cudaStream_t st) {
     Plan pl;
@@ -408,7 +480,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(qmm_gemv_mma_kernel<MT, TPW, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(qmm_gemv_mma_kernel<BITS, MT, TPW, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kSmemLimit);
         if (e != cudaSuccess) return cuda_fail(e, "gemv (mma) smem attribute");
         configured[dev] = true;
@@ -424,15 +496,15 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.k = (int32_t)w.k;
     p.m = (int32_t)m;
     p.groups = (int32_t)(w.k / w.group);
-    p.units = (int32_t)(w.k / kUnit);
-    int us = 0;
-    while ((kUnit << us) < w.group) ++us;
+    p.units = (int32_t)units_of(w);
+    int us = 0;  // units per group = 2^us
+    while ((kUnit << us) < w.group * BITS / 4) ++us;
     p.unit_shift = us;
     p.rb = pl.rb;
     p.ks = pl.ks;
     p.upw = (p.units + pl.ks - 1) / pl.ks;
     p.stages = pl.stages;
-    p.row_bytes = (int32_t)(w.k / 2);
+    p.row_bytes = (int32_t)(w.k * BITS / 8);
     p.quad_stride = pl.quad_stride;
     p.nblocks = (int32_t)((w.n + pl.rb - 1) / pl.rb);
     p.stage_bytes = pl.stage_bytes;
@@ -440,6 +512,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.xp_stride = pl.xp_stride;
     p.err = device_error_word();
     const bool pdl = gemv_pdl_enabled();
+    p.prefetch_weights = (pdl && weights_immutable()) ? 1 : 0;
     const int grid = (int)std::min<int64_t>(p.nblocks, sm_count());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -451,7 +524,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_gemv_mma_kernel<MT, TPW, CW>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_gemv_mma_kernel<BITS, MT, TPW, CW>, p);
     count_launch();
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? QMM_OK : cuda_fail(e, "gemv (mma) launch");
@@ -461,9 +534,9 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
 
 
 bool gemv_mma_supported(const qmm_weight &w, int64_t m) {
-    if (w.bits != 4 || m < 1 || m > 16) return false;
+    if ((w.bits != 4 && w.bits != 8) || m < 1 || m > 16) return false;
     if (w.k % gemvtc::kUnit != 0 || w.group % gemvtc::kUnit != 0) return false;
-    const int per = w.group / gemvtc::kUnit;
+    const int per = w.group * w.bits / 4 / gemvtc::kUnit;  // units per group
     if ((per & (per - 1)) != 0) return false;
     if (w.n % 8 != 0 || w.k > (1 << 20) || w.n > ((int64_t)1 << 31)) return false;
     // Scale/offset blocks are copied in 16-byte pieces.
@@ -476,9 +549,14 @@ qmm_status launch_gemv_mma(const qmm_weight &w, const uint16_t *x, int64_t m, co
                            uint16_t *y, cudaStream_t st) {
     gemvtc::Plan pl;
     if (!gemvtc::plan_for(w, m, pl)) return fail(QMM_ERR_UNSUPPORTED, "gemv (mma): layout does not fit shared memory");
+    if (w.bits == 8) {
+        if (m <= 8)
+            return pl.tpw == 2 ? gemvtc::launch_t<8, 1, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<8, 1, 1, 16>(w, x, m, ep, y, st);
+        return pl.tpw == 2 ? gemvtc::launch_t<8, 2, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<8, 2, 1, 16>(w, x, m, ep, y, st);
+    }
     if (m <= 8)
-        return pl.tpw == 2 ? gemvtc::launch_t<1, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<1, 1, 16>(w, x, m, ep, y, st);
-    return pl.tpw == 2 ? gemvtc::launch_t<2, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<2, 1, 16>(w, x, m, ep, y, st);
+        return pl.tpw == 2 ? gemvtc::launch_t<4, 1, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<4, 1, 1, 16>(w, x, m, ep, y, st);
+    return pl.tpw == 2 ? gemvtc::launch_t<4, 2, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<4, 2, 1, 16>(w, x, m, ep, y, st);
 }
 
 }  // namespace qmm

@@ -27,6 +27,10 @@ void count_launch(uint64_t n = 1);
 // previous kernel of its stream (on unless QMM_GEMV_PDL=0; read once).
 bool gemv_pdl_enabled();
 
+// Whether the caller declared that no kernel writes packed weights, scales or
+// offsets while the library uses them (qmm_set_weights_immutable).
+bool weights_immutable();
+
 // Test support: the GEMM's withheld k-block (-1: none) and wait limit for the
 // next launches (qmm_debug_gemm_stall).
 void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns);

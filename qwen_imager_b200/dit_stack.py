@@ -430,10 +430,18 @@ class DitStack:
         if x.shape != (cfg.tokens, cfg.hidden):
             raise ValueError(f"hidden state {tuple(x.shape)} is not [{cfg.tokens}, {cfg.hidden}]")
         self._buffers(x)
-        mods = self.modulations(temb, timers)
-        if self.tp.sequence_parallel:
-            return self._forward_sequence_parallel(x, mods, timers)
-        return self._forward_replicated(x, mods, timers)
+        # The stack's weights are only read once loaded: the streaming GEMVs
+        # may fetch them before the kernel ahead of them completes.
+        lib = _lib.load() if x.device.type == "cuda" else None
+        prev = lib.qmm_set_weights_immutable(1) if lib else 0
+        try:
+            mods = self.modulations(temb, timers)
+            if self.tp.sequence_parallel:
+                return self._forward_sequence_parallel(x, mods, timers)
+            return self._forward_replicated(x, mods, timers)
+        finally:
+            if lib:
+                lib.qmm_set_weights_immutable(prev)
 
     def _stream_rows(self, lo: int, hi: int):
         """(slice of [lo, hi) relative to lo, stream) for the stream segments of token rows [lo, hi)."""

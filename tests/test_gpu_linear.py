@@ -200,5 +200,5 @@ def test_argument_errors_are_reported():
     assert lib.qmm_linear_ex(ctypes.byref(w), x.data_ptr(), 4, None, y.data_ptr(), 9, None) == _lib.QMM_ERR_INVALID_ARGUMENT
     with pytest.raises(_lib.QmmError):
         lin.forward(torch.zeros((4, 100), dtype=torch.bfloat16, device="cuda"))
-    with pytest.raises(_lib.QmmError):
-        lin.forward(torch.zeros((4, 128), dtype=torch.float32, device="cuda"))
+    with pytest.raises(_lib.QmmError):  # f16 activations: neither the bf16 kernels nor the f32 route
+        lin.forward(torch.zeros((4, 128), dtype=torch.float16, device="cuda"))
