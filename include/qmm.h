@@ -245,14 +245,16 @@ QMM_API uint64_t qmm_static_scratch_bytes(void);
 QMM_API qmm_status qmm_device_error(void *stream, uint32_t *code_out);
 
 /*
- * Test support for the bounded waits (no counterpart in quant.rs): for GEMM
- * launches made after the call, in this process, every CTA's copy producer
- * stops before its `withhold_block`-th k-block (-1: never), and every wait in
- * the GEMM gives up after `wait_limit_ns` (1 ms .. 4 s; 0: the default 4 s).
- * The waits for the withheld block then run out: the launch ends early with
- * its output incomplete, having drained its own copies and MMAs and freed
- * its tensor memory, and qmm_device_error reports QMM_ERR_TIMEOUT.  Call
- * qmm_debug_gemm_stall(-1, 0) to restore normal launches.
+ * Test support for the bounded waits (no counterpart in quant.rs): GEMM
+ * launches made after the call, on the current device, use a test
+ * instantiation of the kernel in which every CTA's copy producer stops before
+ * its `withhold_block`-th k-block (-1: never) and every wait gives up after
+ * `wait_limit_ns` (1 ms .. 4 s; 0: the default 4 s).  The waits for the
+ * withheld block then run out: the launch ends early with its output
+ * incomplete, having drained its own copies and MMAs and freed its tensor
+ * memory, and qmm_device_error reports QMM_ERR_TIMEOUT.  Synchronous (it
+ * writes a device variable).  qmm_debug_gemm_stall(-1, 0) restores normal
+ * launches.
  */
 QMM_API qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns);
 

@@ -79,17 +79,6 @@ int sm_count() {
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 namespace {
-std::atomic<int32_t> g_stall_block{-1};
-std::atomic<uint64_t> g_stall_wait_ns{0};
-}  // namespace
-
-void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns) {
-    *withhold = g_stall_block.load(std::memory_order_relaxed);
-    const uint64_t w = g_stall_wait_ns.load(std::memory_order_relaxed);
-    *wait_ns = w ? w : kWaitLimitNs;
-}
-
-namespace {
 std::atomic<int32_t> g_weights_immutable{0};
 }  // namespace
 
@@ -152,9 +141,9 @@ qmm_status qmm_debug_gemm_stall(int32_t withhold_block, uint64_t wait_limit_ns) 
     if (wait_limit_ns != 0 && (wait_limit_ns < 1000000ull || wait_limit_ns > qmm::kWaitLimitNs))
         return fail(QMM_ERR_INVALID_ARGUMENT, "wait limit %llu ns is outside [1 ms, 4 s]",
                     (unsigned long long)wait_limit_ns);
-    qmm::g_stall_block.store(withhold_block, std::memory_order_relaxed);
-    qmm::g_stall_wait_ns.store(wait_limit_ns, std::memory_order_relaxed);
-    return QMM_OK;
+    qmm_status s = check_device();
+    if (s != QMM_OK) return s;
+    return qmm::gemm_set_stall(withhold_block, wait_limit_ns);
 }
 
 int32_t qmm_set_weights_immutable(int32_t on) {

@@ -1,21 +1,17 @@
 // Fused epilogue: y = residual + gate * act(acc + bias), f32, one bf16 rounding;
-// with kEpiResidualMul in the activation field the residual operand multiplies
-// instead: y = residual * (gate * act(acc + bias)) (the up projection of a
-// SwiGLU MLP times the SiLU-activated gate projection, src/ops.rs:203).
+// with res_mul the residual operand multiplies instead, y = residual * (gate *
+// act(acc + bias)) (a SwiGLU up projection times the SiLU-activated gate
+// projection, src/ops.rs:203).
 // The reference applies these as separate bf16 tensor ops after the linear
 // (image-forger src/quant.rs:157-160 bias; src/dit.rs:88-93 gate and residual).
 #pragma once
 
+#include "qmm.h"
 #include "qmm_common.cuh"
 
 namespace qmm {
 
-// Bit of EpilogueArgs::act (QMM_EPILOGUE_RESIDUAL_MUL): the residual multiplies.
-constexpr int32_t kEpiResidualMul = 0x100;
-constexpr int32_t kEpiActMask = 0xFF;
-
 __device__ __forceinline__ float apply_activation(float t, int act) {
-    act &= kEpiActMask;
     if (act == 1) {  // GELU, tanh approximation
         const float c = 0.7978845608028654f;
         return 0.5f * t * (1.0f + tanhf(c * (t + 0.044715f * t * t * t)));
@@ -28,8 +24,16 @@ struct EpilogueArgs {
     const uint16_t *bias;      // [n] or null
     const uint16_t *gate;      // [n] or null
     const uint16_t *residual;  // [m, n] or null
-    int32_t act;
+    int32_t act;               // qmm_activation
+    int32_t res_mul;           // 1: the residual multiplies (QMM_EPILOGUE_RESIDUAL_MUL)
 };
+
+// The kernels' form of a qmm_epilogue: activation and residual mode decoded
+// once on the host.
+inline EpilogueArgs epilogue_args(const qmm_epilogue &ep) {
+    return EpilogueArgs{ep.bias, ep.gate, ep.residual, ep.activation & 0xFF,
+                        (ep.activation & QMM_EPILOGUE_RESIDUAL_MUL) ? 1 : 0};
+}
 
 // Per-output-feature constants of the epilogue.
 struct FeatureConsts {
@@ -53,7 +57,7 @@ __device__ __forceinline__ float epilogue_value(const EpilogueArgs &e, const Fea
     if (e.gate) t = t * c.gate;
     if (residual_elem) {
         const float r = bf16_bits_to_f32(*residual_elem);
-        t = (e.act & kEpiResidualMul) ? r * t : r + t;
+        t = e.res_mul ? r * t : r + t;
     }
     return t;
 }
@@ -64,7 +68,7 @@ __device__ __forceinline__ float epilogue_value_rv(const EpilogueArgs &e, const 
                                                    float acc, float resid) {
     float t = apply_activation(acc + c.bias, e.act);
     if (e.gate) t = t * c.gate;
-    if (e.residual) t = (e.act & kEpiResidualMul) ? resid * t : resid + t;
+    if (e.residual) t = e.res_mul ? resid * t : resid + t;
     return t;
 }
 

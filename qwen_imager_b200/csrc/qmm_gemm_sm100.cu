@@ -28,6 +28,7 @@
 // Every wait is bounded (qmm_common.cuh): on expiry the CTA records an error
 // code, drains its own in-flight copies and MMAs, frees TMEM and exits.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "qmm_epilogue.cuh"
@@ -111,13 +112,17 @@ struct Params {
     // buffer (needs a residual, no split-K and n % 8 == 0).
     int32_t res_tma;
     uint32_t *err;
-    // Limit of every bounded wait (kWaitLimitNs unless a test shortens it).
+};
+
+// Test support (qmm_debug_gemm_stall), read only by the STALL instantiation
+// of the kernel: every wait gives up after wait_ns, and the copy producer of
+// every CTA stops before its `withhold`-th k-block, so that the waits for that
+// block run out and the error path runs.  Set per device by gemm_set_stall.
+struct StallConfig {
     uint64_t wait_ns;
-    // Test support (qmm_debug_gemm_stall): the producer of every CTA stops
-    // before its `withhold`-th k-block (-1: never), so that the waits for
-    // that block run out and the error path runs.
     int32_t withhold;
 };
+__device__ StallConfig g_stall_cfg = {kWaitLimitNs, -1};
 
 // Byte offset of 16-byte chunk `c` of row `r` in a TMA tile written with
 // 32-byte (4-bit rows) or 64-byte (8-bit rows) swizzling.
@@ -169,7 +174,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
     }
 }
 
-template <int BITS, int T, int SETS, int HALVES, bool PAIR>
+template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false>
 __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w,
@@ -177,6 +182,14 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     const __grid_constant__ CUtensorMap tmap_res, const Params p) {
     using C = Cfg<BITS, T, PAIR>;
     using W = Warps<SETS, HALVES>;
+    // The normal instantiation waits with the constant limit and withholds
+    // nothing (the same code as without test support).
+    uint64_t wait_ns = kWaitLimitNs;
+    int32_t withhold = -1;
+    if constexpr (STALL) {
+        wait_ns = g_stall_cfg.wait_ns;
+        withhold = g_stall_cfg.withhold;
+    }
     constexpr int S = C::kStages;
     constexpr int kASlots = C::kASlots;
     constexpr int kTileRows = PAIR ? 2 * kWRows : kWRows;  // weight rows per (pair) tile
@@ -263,11 +276,13 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             const int n0 = (tile % p.w_tiles) * kTileRows + (int)rank * kWRows;
             const int m0 = (tile / p.w_tiles) * T + (int)rank * C::kXRows;
             for (int kb = kb0; kb < kb0 + nkb; ++kb, ++i) {
-                if ((int32_t)i == p.withhold) {  // test support: this block's copies are never issued
-                    ok = false;
-                    break;
+                if constexpr (STALL) {
+                    if ((int32_t)i == withhold) {  // this block's copies are never issued
+                        ok = false;
+                        break;
+                    }
                 }
-                if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer, p.wait_ns)) {
+                if (!mbar_wait<PAIR>(&sempty[s], ph_s ^ 1, p.err, kErrTimeoutProducer, wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -300,7 +315,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             // Let the copies already issued land before the CTA exits.
             const uint32_t first = i > (uint32_t)S ? i - S : 0;
             for (uint32_t j = first; j < i; ++j)
-                mbar_wait<PAIR>(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain, p.wait_ns);
+                mbar_wait<PAIR>(&full[j % S], (j / S) & 1, p.err, kErrTimeoutDrain, wait_ns);
         }
     } else if (warp == W::kMma) {
         // ---------------------------------------------------------- MMA issuer
@@ -318,7 +333,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             int lt = 0;
             for (int wu = unit; ok && wu < p.num_units; wu += nunits, ++lt) {
                 const int b = lt & 1;
-                ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma, p.wait_ns));
+                ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&acc_empty[b], ((lt >> 1) & 1) ^ 1, p.err, kErrTimeoutMma, wait_ns));
                 if (!ok) break;
                 tc_fence_after_sync();
                 const uint32_t d = tmem + C::kAcc0 + b * T;
@@ -328,7 +343,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     // afull implies full[s] and full[s + 1] as below.
                     for (int kb = 0; kb < nkb; kb += 2) {
                         const int pb = a >> 1;
-                        ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[pb], ph_a, p.err, kErrTimeoutMma, p.wait_ns));
+                        ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[pb], ph_a, p.err, kErrTimeoutMma, wait_ns));
                         if (!ok) break;
                         tc_fence_after_sync();
                         const int s1 = s + 1 == S ? 0 : s + 1;
@@ -369,9 +384,9 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     // complete, so the release/acquire chain through afull[a]
                     // orders the MMA's shared-memory reads after those copies.
                     // A CTA pair also needs the peer's x tile: xfull[s].
-                    ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma, p.wait_ns) &&
+                    ok = __all_sync(0xffffffffu, mbar_wait<PAIR>(&afull[a], ph_a, p.err, kErrTimeoutMma, wait_ns) &&
                                                      (!PAIR || mbar_wait<PAIR>(&xfull[s], ph_s, p.err,
-                                                                               kErrTimeoutMma, p.wait_ns)));
+                                                                               kErrTimeoutMma, wait_ns)));
                     if (!ok) break;
                     tc_fence_after_sync();
                     const uint32_t atm = tmem + C::kASlot0 + a * 32;
@@ -417,7 +432,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     else tc_commit(drain);
                 }
                 __syncwarp();
-                mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain, p.wait_ns);
+                mbar_wait<PAIR>(drain, 0, p.err, kErrTimeoutDrain, wait_ns);
             }
         }
     } else if (warp >= W::kDq0) {
@@ -476,7 +491,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             if (i + SETS < total_blocks) load_meta(nkb_i, n0m, n1m);
             // The codes are dequantized as soon as they land; only the store
             // into the TMEM A slot waits for the MMA that last read the slot.
-            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant, p.wait_ns)) break;
+            if (!mbar_wait<PAIR>(&full[s], ph_s, p.err, kErrTimeoutDequant, wait_ns)) break;
             const uint8_t *pst = smem + C::kPOff + s * C::kPStageBytes;
             constexpr int kV = HALVES == 1 ? 32 : 16;
             uint32_t v[kV];
@@ -485,7 +500,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
             const int ab = p.kpair ? (a >> 1) : a;  // the slot's barrier (shared by a slot pair)
-            if (!mbar_wait<PAIR>(&aempty[ab], ph_a ^ 1, p.err, kErrTimeoutDequant, p.wait_ns)) break;
+            if (!mbar_wait<PAIR>(&aempty[ab], ph_a ^ 1, p.err, kErrTimeoutDequant, wait_ns)) break;
             if constexpr (HALVES == 1) tmem_st_32x32b_x32(tcol + a * 32, v);
             else tmem_st_32x32b_x16(tcol + a * 32, v);
             tc_wait_st();
@@ -535,7 +550,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             const int m0 = (tile / p.w_tiles) * T;
             // The four epilogue warps leave together (they meet at named
             // barriers below): one expired wait ends the loop for all.
-            const bool waited = mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue, p.wait_ns);
+            const bool waited = mbar_wait<PAIR>(&acc_full[b], u & 1, p.err, kErrTimeoutEpilogue, wait_ns);
             if (named_barrier_or(1, kEpiWarps * 32, !waited)) break;
             tc_fence_after_sync();
             const int64_t n = n0 + quad * 32 + lane;
@@ -586,7 +601,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     if (p.res_tma) {
                         // This chunk's residual is in the staging buffer: read
                         // it and overwrite it with the output in place.
-                        mbar_wait<PAIR>(&rfull[eb], (chunk >> 1) & 1, p.err, kErrTimeoutEpilogue, p.wait_ns);
+                        mbar_wait<PAIR>(&rfull[eb], (chunk >> 1) & 1, p.err, kErrTimeoutEpilogue, wait_ns);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             uint16_t &slot = st16[j * kWRows + quad * 32 + lane];
@@ -646,7 +661,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
         }
         if (quad == 0 && lane == 0) {
             // On an early exit a prefetched residual chunk may still be landing.
-            if (res_pending) mbar_wait<PAIR>(&rfull[chunk & 1], (chunk >> 1) & 1, p.err, kErrTimeoutDrain, p.wait_ns);
+            if (res_pending) mbar_wait<PAIR>(&rfull[chunk & 1], (chunk >> 1) & 1, p.err, kErrTimeoutDrain, wait_ns);
             bulk_wait_all();  // the stores have landed before the CTA exits
         }
     }
@@ -746,11 +761,11 @@ static qmm_status make_map_3d_f32(CUtensorMap *map, const void *base, uint64_t i
     return QMM_OK;
 }
 
-template <int BITS, int T, int SETS, int HALVES, bool PAIR>
+template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
                            const qmm_epilogue &ep, uint16_t *y, int splits, float *ws, cudaStream_t st) {
     using C = Cfg<BITS, T, PAIR>;
-    auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR>;
+    auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR, STALL>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -799,7 +814,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.offsets = w.biases;
     p.y = y;
     p.ws = splits > 1 ? ws : nullptr;
-    p.ep = EpilogueArgs{ep.bias, ep.gate, ep.residual, ep.activation};
+    p.ep = epilogue_args(ep);
     p.m = (int32_t)m;
     p.n = (int32_t)w.n;
     p.k = (int32_t)w.k;
@@ -817,7 +832,6 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     p.kpair = (!PAIR && SETS == 4 && HALVES == 1 && C::kASlots == 4 && p.kbs % 2 == 0) ? 1 : 0;
     p.res_tma = res_tma ? 1 : 0;
     p.err = device_error_word();
-    debug_gemm_stall(&p.withhold, &p.wait_ns);
     const int ctas = PAIR ? 2 : 1;
     const int units = (int)std::min<int64_t>(p.num_units, sm_count() / ctas);
     cudaLaunchConfig_t cfg = {};
@@ -847,7 +861,17 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
     return QMM_OK;
 }
 
+std::atomic<bool> g_stall_on{false};
+
 }  // namespace gemm
+
+qmm_status gemm_set_stall(int32_t withhold, uint64_t wait_ns) {
+    const gemm::StallConfig cfg{wait_ns ? wait_ns : kWaitLimitNs, withhold};
+    cudaError_t e = cudaMemcpyToSymbol(gemm::g_stall_cfg, &cfg, sizeof cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm stall configuration");
+    gemm::g_stall_on.store(withhold >= 0 || wait_ns != 0, std::memory_order_relaxed);
+    return QMM_OK;
+}
 
 bool gemm_supported(const qmm_weight &w) {
     if (w.bits != 4 && w.bits != 8) return false;
@@ -884,6 +908,12 @@ qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const 
     // on request: they halve the x traffic per SM but lengthen the A-slot
     // hand-off by a cross-SM round trip, which measured slower on B200.
     pair = pair && w.n > gemm::kWRows && splits == 1;
+    if (gemm::g_stall_on.load(std::memory_order_relaxed) && !pair) {
+        // Test support: the instantiation whose waits and producer follow
+        // the stall configuration (qmm_debug_gemm_stall).
+        return w.bits == 4 ? gemm::launch_t<4, 192, 4, 1, false, true>(w, x, m, ep, y, splits, ws, st)
+                           : gemm::launch_t<8, 192, 4, 1, false, true>(w, x, m, ep, y, splits, ws, st);
+    }
     if (w.bits == 4)
         return pair ? gemm::launch_t<4, 192, 4, 1, true>(w, x, m, ep, y, 1, nullptr, st)
                     : gemm::launch_t<4, 192, 4, 1, false>(w, x, m, ep, y, splits, ws, st);

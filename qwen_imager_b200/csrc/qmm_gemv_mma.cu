@@ -491,7 +491,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.scales = w.scales;
     p.offsets = w.biases;
     p.y = y;
-    p.ep = EpilogueArgs{ep.bias, ep.gate, ep.residual, ep.activation};
+    p.ep = epilogue_args(ep);
     p.n = w.n;
     p.k = (int32_t)w.k;
     p.m = (int32_t)m;

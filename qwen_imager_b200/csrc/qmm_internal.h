@@ -31,9 +31,10 @@ bool gemv_pdl_enabled();
 // offsets while the library uses them (qmm_set_weights_immutable).
 bool weights_immutable();
 
-// Test support: the GEMM's withheld k-block (-1: none) and wait limit for the
-// next launches (qmm_debug_gemm_stall).
-void debug_gemm_stall(int32_t *withhold, uint64_t *wait_ns);
+// Test support (qmm_debug_gemm_stall): GEMM launches made after the call on
+// the current device withhold k-block `withhold` (-1: none) and wait at most
+// wait_ns (0: the default limit); (-1, 0) restores normal launches.
+qmm_status gemm_set_stall(int32_t withhold, uint64_t wait_ns);
 
 // Launchers.  Arguments are validated by the caller (qmm_api.cu).
 qmm_status launch_dequantize(const qmm_weight &w, void *dst, int32_t dtype, cudaStream_t st);
