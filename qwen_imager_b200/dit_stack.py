@@ -293,11 +293,12 @@ class TensorParallel:
     collective's kernels have SMs to run on."""
 
     def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 1, comm_sms: int = 16,
-                 sequence_parallel: bool = True):
+                 sequence_parallel: bool = True, sp_chunks: int = 1):
         self.rank, self.world, self.group = rank, world, group
         self.overlap_chunks = overlap_chunks if world > 1 else 1
         self.comm_sms = comm_sms
         self.sequence_parallel = sequence_parallel and world > 1
+        self.sp_chunks = sp_chunks if self.sequence_parallel else 1
 
     @classmethod
     def from_env(cls, **kw):
@@ -322,30 +323,33 @@ class TensorParallel:
         import torch.distributed as dist
         return dist.all_reduce(t, group=self.group, async_op=True)
 
-    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = False):
         """out [M / world, ...] = rows [rank M / world, (rank + 1) M / world) of
-        the sum over ranks of inp [M, ...]."""
+        the sum over ranks of inp [M, ...].  async_op: enqueued after the
+        current stream's work; the returned handle's wait() makes the current
+        stream wait for it (None when it already ran)."""
         if self.world == 1:
             out.copy_(inp)
-            return
+            return None
         import torch.distributed as dist
         if self._native(inp):
-            dist.reduce_scatter_tensor(out, inp, group=self.group)
-        else:
-            t = inp.clone()
-            dist.all_reduce(t, group=self.group)
-            out.copy_(t.chunk(self.world)[self.rank])
+            return dist.reduce_scatter_tensor(out, inp, group=self.group, async_op=async_op)
+        t = inp.clone()
+        dist.all_reduce(t, group=self.group)
+        out.copy_(t.chunk(self.world)[self.rank])
+        return None
 
-    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
-        """out [world * L, ...] = the ranks' inp [L, ...] in rank order."""
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor, async_op: bool = False):
+        """out [world * L, ...] = the ranks' inp [L, ...] in rank order
+        (async_op as for reduce_scatter)."""
         if self.world == 1:
             out.copy_(inp)
-            return
+            return None
         import torch.distributed as dist
         if self._native(inp):
-            dist.all_gather_into_tensor(out, inp, group=self.group)
-        else:
-            dist.all_gather(list(out.chunk(self.world)), inp.contiguous(), group=self.group)
+            return dist.all_gather_into_tensor(out, inp, group=self.group, async_op=async_op)
+        dist.all_gather(list(out.chunk(self.world)), inp.contiguous(), group=self.group)
+        return None
 
 
 class DitStack:
@@ -354,8 +358,8 @@ class DitStack:
     def __init__(self, cfg: StackConfig, blocks: List[List[StreamWeights]], tp: TensorParallel,
                  run_linear: RunLinear = cuda_linear, attention: Optional[Callable] = None):
         cfg.check_world(tp.world)
-        if tp.sequence_parallel and cfg.tokens % tp.world:
-            raise ValueError(f"{cfg.tokens} tokens do not split over {tp.world} ranks")
+        if tp.sequence_parallel and cfg.tokens % (tp.world * tp.sp_chunks):
+            raise ValueError(f"{cfg.tokens} tokens do not split into {tp.sp_chunks} chunks over {tp.world} ranks")
         self.cfg, self.blocks, self.tp = cfg, blocks, tp
         self.run_linear = run_linear
         self.attention = attention or _sdpa
@@ -454,59 +458,107 @@ class DitStack:
         return out
 
     def _forward_sequence_parallel(self, x, mods, timers):
+        """Sequence-parallel form in tp.sp_chunks token chunks.  Chunk c holds
+        tokens [c M/C, (c+1) M/C) and this rank owns the rank-th 1/world of
+        each chunk.  With one chunk every collective runs in turn with the
+        computation; with several, each chunk's reduce-scatter and all-gather
+        run on the collective stream while the next chunk's linears run (the
+        steps between two attentions are per token, so the chunks only meet
+        at attention), and the GEMMs leave tp.comm_sms SMs to the
+        collectives."""
         cfg, tp = self.cfg, self.tp
         bufs = self._bufs[1]
         qkv, attn, hid, part = bufs["qkv"], bufs["attn"], bufs["hid"], bufs["part"]
         nfull, xl, nl, red = bufs["nfull"], bufs["xl"], bufs["nl"], bufs["red"]
-        local = cfg.tokens // tp.world
-        lo = tp.rank * local
-        segs = self._stream_rows(lo, lo + local)
-        rows = (slice(0, cfg.img_tokens), slice(cfg.img_tokens, cfg.tokens))
+        nc = tp.sp_chunks
+        span = cfg.tokens // nc             # tokens per chunk
+        piece = span // tp.world            # this rank's tokens of a chunk
+        chunk = [slice(c * span, (c + 1) * span) for c in range(nc)]
+        own = [slice(c * piece, (c + 1) * piece) for c in range(nc)]  # the chunk's piece in xl / nl / red
+        first = [c * span + tp.rank * piece for c in range(nc)]        # its first token
+        # (rows of xl, stream) of each piece, and (token rows, stream) of each chunk
+        segs = [[(slice(c * piece + r.start, c * piece + r.stop), s)
+                 for r, s in self._stream_rows(first[c], first[c] + piece)] for c in range(nc)]
+        rows = [[(slice(c * span + r.start, c * span + r.stop), s)
+                 for r, s in self._stream_rows(c * span, (c + 1) * span)] for c in range(nc)]
         dl = cfg.heads * cfg.head_dim // tp.world
-        xl.copy_(x[lo:lo + local])
+        overlap = nc > 1
+        for c in range(nc):
+            xl[own[c]].copy_(x[first[c]:first[c] + piece])
+
+        def waitall(works):
+            with timers.span("comm"):
+                for w in works:
+                    if w is not None:
+                        w.wait()
+
         with timers.span("other"):
-            for r, s in segs:
-                _modulate(xl[r], mods[0, s, 0], mods[0, s, 1], nl[r])
+            for c in range(nc):
+                for r, s in segs[c]:
+                    _modulate(xl[r], mods[0, s, 0], mods[0, s, 1], nl[r])
         with timers.span("comm"):
-            tp.all_gather(nfull, nl)
-        nb = len(self.blocks)
-        for b, blk in enumerate(self.blocks):
-            m = mods[b]
-            with timers.span("linear"):
-                for s in range(2):
-                    self.run_linear(blk[s].qkv, nfull[rows[s]], out=qkv[rows[s]])
-            with timers.span("attention"):
-                self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
-            with timers.span("linear"):
-                for s in range(2):
-                    self.run_linear(blk[s].out, attn[rows[s]], gate=m[s, 2], bias=None, out=part[rows[s]])
-            with timers.span("comm"):
-                tp.reduce_scatter(red, part)
-            with timers.span("other"):
-                for r, s in segs:
-                    _residual_modulate(xl[r], red[r], blk[s].out_bias, m[s, 2], m[s, 3], m[s, 4], nl[r])
-            with timers.span("comm"):
-                tp.all_gather(nfull, nl)
-            with timers.span("linear"):
-                for s in range(2):
-                    self.run_linear(blk[s].up, nfull[rows[s]], activation="gelu_tanh", out=hid[rows[s]])
-                for s in range(2):
-                    self.run_linear(blk[s].down, hid[rows[s]], gate=m[s, 5], bias=None, out=part[rows[s]])
-            with timers.span("comm"):
-                tp.reduce_scatter(red, part)
-            last = b + 1 == nb
-            with timers.span("other"):
-                for r, s in segs:
-                    if last:
-                        _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], None, None, None)
-                    else:
-                        _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], mods[b + 1, s, 0],
-                                           mods[b + 1, s, 1], nl[r])
-            if not last:
-                with timers.span("comm"):
-                    tp.all_gather(nfull, nl)
+            for c in range(nc):
+                tp.all_gather(nfull[chunk[c]], nl[own[c]])
+        ag = [None] * nc
+        budget = None
+        if overlap and x.device.type == "cuda":
+            budget = _lib.load().qmm_set_sm_budget(max(1, _sm_count(x.device) - tp.comm_sms))
+        try:
+            nb = len(self.blocks)
+            for b, blk in enumerate(self.blocks):
+                m = mods[b]
+                for c in range(nc):
+                    waitall([ag[c]])
+                    with timers.span("linear"):
+                        for r, s in rows[c]:
+                            self.run_linear(blk[s].qkv, nfull[r], out=qkv[r])
+                with timers.span("attention"):
+                    self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
+                rs = []
+                for c in range(nc):
+                    with timers.span("linear"):
+                        for r, s in rows[c]:
+                            self.run_linear(blk[s].out, attn[r], gate=m[s, 2], bias=None, out=part[r])
+                    with timers.span("comm"):
+                        rs.append(tp.reduce_scatter(red[own[c]], part[chunk[c]], async_op=overlap))
+                ag = []
+                for c in range(nc):
+                    waitall([rs[c]])
+                    with timers.span("other"):
+                        for r, s in segs[c]:
+                            _residual_modulate(xl[r], red[r], blk[s].out_bias, m[s, 2], m[s, 3], m[s, 4], nl[r])
+                    with timers.span("comm"):
+                        ag.append(tp.all_gather(nfull[chunk[c]], nl[own[c]], async_op=overlap))
+                rs = []
+                for c in range(nc):
+                    waitall([ag[c]])
+                    with timers.span("linear"):
+                        for r, s in rows[c]:
+                            self.run_linear(blk[s].up, nfull[r], activation="gelu_tanh", out=hid[r])
+                        for r, s in rows[c]:
+                            self.run_linear(blk[s].down, hid[r], gate=m[s, 5], bias=None, out=part[r])
+                    with timers.span("comm"):
+                        rs.append(tp.reduce_scatter(red[own[c]], part[chunk[c]], async_op=overlap))
+                last = b + 1 == nb
+                ag = [None] * nc
+                for c in range(nc):
+                    waitall([rs[c]])
+                    with timers.span("other"):
+                        for r, s in segs[c]:
+                            if last:
+                                _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], None, None, None)
+                            else:
+                                _residual_modulate(xl[r], red[r], blk[s].down_bias, m[s, 5], mods[b + 1, s, 0],
+                                                   mods[b + 1, s, 1], nl[r])
+                    if not last:
+                        with timers.span("comm"):
+                            ag[c] = tp.all_gather(nfull[chunk[c]], nl[own[c]], async_op=overlap)
+        finally:
+            if budget is not None:
+                _lib.load().qmm_set_sm_budget(budget)
         with timers.span("comm"):
-            tp.all_gather(x, xl)
+            for c in range(nc):
+                tp.all_gather(x[chunk[c]], xl[own[c]])
         return x
 
     def _forward_replicated(self, x, mods, timers):

@@ -104,18 +104,19 @@ def _inputs(cfg, seed):
     return x, temb
 
 
-def _run_stack(cfg, rank, world, seed, sp=True):
+def _run_stack(cfg, rank, world, seed, sp=True, chunks=1):
     x, temb = _inputs(cfg, seed)
-    stack = DitStack.from_full(cfg, _full_weights(cfg, seed), TensorParallel(rank, world, sequence_parallel=sp),
+    stack = DitStack.from_full(cfg, _full_weights(cfg, seed),
+                               TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks),
                                run_linear=oracle_run_linear)
     return stack.forward(x, temb)
 
 
-def _gloo_rank(rank, world, port, seed, path, sp=True):
+def _gloo_rank(rank, world, port, seed, path, sp=True, chunks=1):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        y = _run_stack(SMALL, rank, world, seed, sp)
+        y = _run_stack(SMALL, rank, world, seed, sp, chunks)
         torch.save(y, f"{path}.{rank}")
     finally:
         dist.destroy_process_group()
@@ -140,6 +141,33 @@ def test_gloo_stack_matches_one_rank(tmp_path, world, sp):
         assert mx <= bar and mean <= 1e-3, (r, mx, mean)
     for r in range(1, world):  # every rank ends with the same whole hidden state
         assert torch.equal(torch.load(f"{path}.0"), torch.load(f"{path}.{r}"))
+
+
+def test_chunked_sequence_parallel_equals_unchunked(tmp_path):
+    # Two token chunks pipeline the collectives against the linears; with two
+    # ranks every sum is one addition in either form, so the result is
+    # bit-identical (with more ranks the reduction order of the collective
+    # may differ with the message size; see the next test).
+    seed, world = 13, 2
+    outs = {}
+    for chunks in (1, 2):
+        path = str(tmp_path / f"c{chunks}")
+        mp.start_processes(_gloo_rank, args=(world, _free_port(), seed, path, True, chunks), nprocs=world,
+                           start_method="spawn")
+        outs[chunks] = [torch.load(f"{path}.{r}") for r in range(world)]
+    for r in range(world):
+        assert torch.equal(outs[1][r], outs[2][r]), r
+
+
+def test_chunked_sequence_parallel_four_ranks_matches_one_rank(tmp_path):
+    seed, world = 13, 4
+    ref = _run_stack(SMALL, 0, 1, seed)
+    path = str(tmp_path / "y")
+    mp.start_processes(_gloo_rank, args=(world, _free_port(), seed, path, True, 2), nprocs=world,
+                       start_method="spawn")
+    for r in range(world):
+        mx, mean = rel_errors(_bits16(torch.load(f"{path}.{r}")), ref.float().numpy())
+        assert mx <= TP_MAX_REL and mean <= 1e-3, (r, mx, mean)
 
 
 def test_sequence_parallel_needs_tokens_divisible_by_ranks():

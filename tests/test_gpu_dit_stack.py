@@ -50,7 +50,7 @@ def test_stack_cuda_matches_oracle_stack(cfg):
     assert mx <= 1e-2 and mean <= 1e-3, (mx, mean)
 
 
-def _nccl_rank(rank, world, port, seed, path, sp):
+def _nccl_rank(rank, world, port, seed, path, sp, chunks=1):
     import datetime
 
     import torch.distributed as dist
@@ -61,7 +61,7 @@ def _nccl_rank(rank, world, port, seed, path, sp):
         x, temb = _inputs(SMALL_TP, seed)
         dev = torch.device("cuda", rank)
         stack = DitStack.from_full(SMALL_TP, _weights(SMALL_TP, seed, dev),
-                                   TensorParallel(rank, world, sequence_parallel=sp))
+                                   TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks))
         y = stack.forward(x.to(dev), temb.to(dev))
         torch.cuda.synchronize()
         torch.save(y.cpu(), f"{path}.{rank}")
@@ -72,9 +72,10 @@ def _nccl_rank(rank, world, port, seed, path, sp):
 
 # Sequence-parallel TP-N meets the one-rank bar; the replicated form sums the
 # whole hidden state in bf16 (see tests/test_dit_stack.py) and gets twice it.
-@pytest.mark.parametrize("world,sp", [(2, True), (4, True), (8, True), (2, False)],
-                         ids=["sp2", "sp4", "sp8", "replicated2"])
-def test_stack_nccl_matches_one_rank(tmp_path, world, sp):
+@pytest.mark.parametrize("world,sp,chunks", [(2, True, 1), (4, True, 1), (8, True, 1), (2, False, 1),
+                                              (2, True, 2), (8, True, 2)],
+                         ids=["sp2", "sp4", "sp8", "replicated2", "sp2-chunked", "sp8-chunked"])
+def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     seed = 23
@@ -85,7 +86,7 @@ def test_stack_nccl_matches_one_rank(tmp_path, world, sp):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     path = str(tmp_path / "y")
-    mp.start_processes(_nccl_rank, args=(world, port, seed, path, sp), nprocs=world, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(world, port, seed, path, sp, chunks), nprocs=world, start_method="spawn")
     bar = 1e-2 if sp else 2e-2
     for r in range(world):
         mx, mean = rel_errors(_bits16(torch.load(f"{path}.{r}")), ref.float().cpu().numpy())
