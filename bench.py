@@ -601,11 +601,14 @@ def run_stack(args, rank, world, device):
     ms = elapsed / args.steps
     clocks = sampler.summary()
 
-    # One more step with CUDA events around every op category.
+    # One more step with CUDA events around every op category, inside an NVTX
+    # range ("dit_step") so that a profiler can capture exactly one step.
     timers = Timers(enabled=True)
     if dist:
         tdist.barrier()
+    torch.cuda.nvtx.range_push("dit_step")
     step(timers)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     parts = {k: round(v, 3) for k, v in timers.totals_ms().items()}
     lin_flops = cfg.blocks * cfg.linear_flops_per_block()
