@@ -626,7 +626,9 @@ def run_stack(args, rank, world, device):
     peak, peak_source = choose_peak(layer_region / max(1, len(layers)), layer_sampler.summary())
     achieved = dom["alg_flops"] / (dom["kernel_us"] * 1e-6) / 1e12
     roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
+            "frac": round(achieved / peak, 4),
+            # the committed capture is of the one-rank shape; the shards of N > 1 are other shapes
+            "traffic": profile_traffic(args.workload) if world == 1 else None,
             "kernel": f"{dom['layer']} GEMM {dom['m']}x{dom['k']}x{dom['n']} {cfg.bits}-bit ({dom['epilogue']}), "
                       f"rank 0",
             "kernel_ms": round(dom["kernel_us"] * 1e-3, 5), "peak_source": peak_source,
