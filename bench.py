@@ -84,6 +84,8 @@ def parse():
     p.add_argument("--sp-chunks", type=int, default=1,
                    help="dit_* on N > 1: token chunks whose reduce-scatter / all-gather overlap the other chunks' "
                         "linears (1 = none)")
+    p.add_argument("--peer", action="store_true",
+                   help="dit_* on N > 1: the sequence-parallel collectives over peer memory (qmm_tp_*) instead of NCCL")
     p.add_argument("--comm-sms", type=int, default=16,
                    help="dit_* with --sp-chunks > 1: SMs the GEMMs leave to the collectives")
     a = p.parse_args()
@@ -510,7 +512,7 @@ def choose_peak(region_s, clocks):
 TP_PARITY_CFG = dict(img_tokens=448, txt_tokens=64, blocks=2, hidden=1024, heads=8, head_dim=128, ffn=2048)
 
 
-def tp_parity(bits, rank, world, device, sp_chunks=1):
+def tp_parity(bits, rank, world, device, sp_chunks=1, peer=False):
     """Untimed check on every rank: a small stack sharded over the N ranks
     (sequence-parallel form, NCCL) against the same weights on this rank
     alone; max|d| / max|ref| <= 1e-2 and mean|d| / max|ref| <= 1e-3."""
@@ -532,8 +534,8 @@ def tp_parity(bits, rank, world, device, sp_chunks=1):
     x = torch.randn((cfg.tokens, cfg.hidden), generator=g).to(torch.bfloat16).to(device)
     temb = torch.randn((cfg.hidden,), generator=g).to(torch.bfloat16).to(device)
     ref = DitStack.from_full(cfg, full, TensorParallel()).forward(x.clone(), temb).float()
-    got = DitStack.from_full(cfg, full, TensorParallel(rank, world, sp_chunks=sp_chunks)).forward(x.clone(),
-                                                                                                  temb).float()
+    got = DitStack.from_full(cfg, full, TensorParallel(rank, world, sp_chunks=sp_chunks, peer=peer)).forward(
+        x.clone(), temb).float()
     torch.cuda.synchronize()
     d = (got - ref).abs()
     scale = ref.abs().max()
@@ -541,8 +543,9 @@ def tp_parity(bits, rank, world, device, sp_chunks=1):
                         dtype=torch.float64, device=device)
     tdist.all_reduce(errs, op=tdist.ReduceOp.MAX)
     mx, mean, mm = (float(v) for v in errs.tolist())
-    return {"world": world, "form": f"sequence-parallel (reduce-scatter + all-gather, NCCL bf16), "
-                                     f"{sp_chunks} token chunk(s)",
+    form = ("sequence-parallel, peer-memory exchange (qmm_tp_*: f32 sum of the partials)" if peer else
+            f"sequence-parallel (reduce-scatter + all-gather, NCCL bf16), {sp_chunks} token chunk(s)")
+    return {"world": world, "form": form,
             "max_rel": round(mx, 6), "mean_rel": round(mean, 7), "mean_abs_over_mean_abs": round(mm, 6),
             "bar": {"max_rel": 1e-2, "mean_rel": 1e-3}, "pass": bool(mx <= 1e-2 and mean <= 1e-3),
             "normalised_by": "max|ref| (the reference test's metric); worst rank",
@@ -558,7 +561,7 @@ def run_stack(args, rank, world, device):
 
     cfg = STACKS[args.workload]
     tp = TensorParallel(rank, world, overlap_chunks=args.overlap_chunks, comm_sms=args.comm_sms,
-                        sequence_parallel=not args.replicated, sp_chunks=args.sp_chunks)
+                        sequence_parallel=not args.replicated, sp_chunks=args.sp_chunks, peer=args.peer)
     stack = DitStack.random(cfg, tp, seed=1, device=device)
     g = torch.Generator(device=device)
     g.manual_seed(1234)  # the same hidden state and timestep on every rank
@@ -676,7 +679,8 @@ def run_stack(args, rank, world, device):
                        "memory and the new hidden state read back, every step (bytes per rank)"}
     if device_error(device):
         raise RuntimeError("device-side wait expired during the timed region")
-    parity = tp_parity(cfg.bits, rank, world, device, args.sp_chunks) if (dist and not args.no_parity) else None
+    parity = (tp_parity(cfg.bits, rank, world, device, args.sp_chunks, args.peer)
+              if (dist and not args.no_parity) else None)
     breakdown = {"ms_" + k: v for k, v in parts.items()}
     lin_ms = parts.get("linear", 0.0) + parts.get("rowpar_linear+all_reduce", 0.0)
     breakdown.update({
@@ -902,7 +906,7 @@ def main_stack(args, world, rank, local):
               "tokens": cfg.tokens, "hidden": cfg.hidden, "blocks": cfg.blocks, "bits": cfg.bits, "group": cfg.group,
               "parallelism": f"tp{world} (column-parallel QKV/up/modulation, row-parallel out/down; {form})"
                              if world > 1 else "tp1",
-              "overlap_chunks": args.overlap_chunks, "sp_chunks": args.sp_chunks,
+              "overlap_chunks": args.overlap_chunks, "sp_chunks": args.sp_chunks, "peer_collectives": args.peer,
               "l2": "weights of every step (GBs) far exceed L2 (no flush); per-layer timings walk over the blocks' "
                     "weights (inputs + weights of each launch > 126 MB)"}
     common = {"metric": STACK_METRIC, "unit": "ms", "steps": args.steps, "warmup": args.warmup,

@@ -212,6 +212,67 @@ QMM_API qmm_status qmm_residual_layernorm_modulate(uint16_t *x, int64_t rows, in
                                            void *stream);
 
 /*
+ * Tensor-parallel collectives of the sequence-parallel DiT stack over peer
+ * memory (NVLink), fused with the residual update and the next LayerNorm +
+ * modulation.  No counterpart in quant.rs (the reference runs on one device);
+ * they replace, per row-parallel layer, an NCCL reduce-scatter, the
+ * residual + norm kernel and an NCCL all-gather.
+ *
+ * Every rank holds three symmetric buffers (allocated so that every rank can
+ * address every rank's copy, e.g. a symmetric allocation or CUDA IPC):
+ *   part     bf16 [world * rows, hidden]  this rank's gated row-parallel partials
+ *   gathered bf16 [world * rows, hidden]  the normalised input of the next
+ *                                         column-parallel linear, whole
+ *   counters uint64 [4], zero at first use
+ * Rank r owns tokens [r * rows, (r + 1) * rows).  Per layer, on every rank and
+ * in the same order: qmm_tp_signal_ready (this rank's `part` is complete),
+ * qmm_tp_reduce_norm_gather with the layer's epoch (1, 2, ... counting these
+ * calls), qmm_tp_wait_gathered with the same epoch.  Every wait inside is
+ * bounded (4 s); on expiry the kernels skip their work and qmm_device_error
+ * reports QMM_ERR_TIMEOUT.
+ */
+#define QMM_TP_MAX_RANKS 8
+
+typedef struct qmm_tp_peers {
+    int32_t world;
+    int32_t rank;
+    uint16_t *part[QMM_TP_MAX_RANKS];
+    uint16_t *gathered[QMM_TP_MAX_RANKS];
+    uint64_t *counters[QMM_TP_MAX_RANKS];
+} qmm_tp_peers;
+
+/* Per-stream vectors of the residual update and the next norm (index 0: the
+ * rows before `split`, 1: from `split` on), bf16 [hidden] each; bias and gate
+ * may be NULL (the gate multiplies only the bias). */
+typedef struct qmm_tp_norm {
+    const uint16_t *bias[2];
+    const uint16_t *gate[2];
+    const uint16_t *shift[2];
+    const uint16_t *scale[2];
+    int64_t split;
+    float eps;
+} qmm_tp_norm;
+
+/* This rank's `part` is complete: tells every rank (one tiny kernel on `stream`). */
+QMM_API qmm_status qmm_tp_signal_ready(const qmm_tp_peers *peers, void *stream);
+
+/*
+ * For this rank's `rows` tokens (x: bf16 [rows, hidden], hidden 256, 512, 1024,
+ * 3072 or 4096): with `reduce`, waits for every rank's signal of this epoch and
+ * sets x = bf16(x + sum over ranks of part + gate * bias) (f32 sum, one
+ * rounding); with `normalize`, stores bf16(LayerNorm(x) * (1 + scale) + shift)
+ * into every rank's `gathered` at the tokens' rows.
+ */
+QMM_API qmm_status qmm_tp_reduce_norm_gather(const qmm_tp_peers *peers, uint64_t epoch, int64_t rows,
+                                     int64_t hidden, uint16_t *x, const qmm_tp_norm *norm,
+                                     int32_t reduce, int32_t normalize, void *stream);
+
+/* Waits (one tiny kernel on `stream`) until every rank has finished the
+ * epoch's qmm_tp_reduce_norm_gather: `gathered` is complete and no rank still
+ * reads this rank's `part`. */
+QMM_API qmm_status qmm_tp_wait_gathered(const qmm_tp_peers *peers, uint64_t epoch, void *stream);
+
+/*
  * qmm_linear_splitk with the f32 scratch in a static device array of the
  * library (qmm_static_scratch_bytes() = 16 MiB, held by every GPU that loads
  * the library until exit) instead of a caller workspace: allocates nothing.

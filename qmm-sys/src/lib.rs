@@ -75,6 +75,31 @@ pub struct qmm_epilogue {
     pub activation: i32,
 }
 
+pub const QMM_TP_MAX_RANKS: i32 = 8;
+
+/// The symmetric buffers of a tensor-parallel group as every rank sees them.
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct qmm_tp_peers {
+    pub world: i32,
+    pub rank: i32,
+    pub part: [*mut u16; 8],
+    pub gathered: [*mut u16; 8],
+    pub counters: [*mut u64; 8],
+}
+
+/// Per-stream vectors of the residual update and the next norm.
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct qmm_tp_norm {
+    pub bias: [*const u16; 2],
+    pub gate: [*const u16; 2],
+    pub shift: [*const u16; 2],
+    pub scale: [*const u16; 2],
+    pub split: i64,
+    pub eps: f32,
+}
+
 #[link(name = "qmm")]
 extern "C" {
     pub fn qmm_abi_version() -> i32;
@@ -101,6 +126,11 @@ extern "C" {
                                            bias: *const u16, gate: *const u16, shift: *const u16,
                                            scale: *const u16, eps: f32, out: *mut u16,
                                            stream: *mut c_void) -> qmm_status;
+    pub fn qmm_tp_signal_ready(peers: *const qmm_tp_peers, stream: *mut c_void) -> qmm_status;
+    pub fn qmm_tp_reduce_norm_gather(peers: *const qmm_tp_peers, epoch: u64, rows: i64, hidden: i64, x: *mut u16,
+                                     norm: *const qmm_tp_norm, reduce: i32, normalize: i32,
+                                     stream: *mut c_void) -> qmm_status;
+    pub fn qmm_tp_wait_gathered(peers: *const qmm_tp_peers, epoch: u64, stream: *mut c_void) -> qmm_status;
     pub fn qmm_linear_splitk_static(w: *const qmm_weight, x: *const u16, m: i64, ep: *const qmm_epilogue,
                                     y: *mut u16, splits: i32, stream: *mut c_void) -> qmm_status;
     pub fn qmm_static_scratch_bytes() -> u64;

@@ -68,6 +68,9 @@ EXPORTED_SYMBOLS = (
     "qmm_binary_version",
     "qmm_debug_gemm_stall",
     "qmm_set_weights_immutable",
+    "qmm_tp_signal_ready",
+    "qmm_tp_reduce_norm_gather",
+    "qmm_tp_wait_gathered",
 )
 
 
@@ -97,6 +100,30 @@ class QmmEpilogue(ctypes.Structure):
         ("gate", ctypes.c_void_p),
         ("residual", ctypes.c_void_p),
         ("activation", ctypes.c_int32),
+    ]
+
+
+QMM_TP_MAX_RANKS = 8
+
+
+class QmmTpPeers(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("part", ctypes.c_void_p * QMM_TP_MAX_RANKS),
+        ("gathered", ctypes.c_void_p * QMM_TP_MAX_RANKS),
+        ("counters", ctypes.c_void_p * QMM_TP_MAX_RANKS),
+    ]
+
+
+class QmmTpNorm(ctypes.Structure):
+    _fields_ = [
+        ("bias", ctypes.c_void_p * 2),
+        ("gate", ctypes.c_void_p * 2),
+        ("shift", ctypes.c_void_p * 2),
+        ("scale", ctypes.c_void_p * 2),
+        ("split", ctypes.c_int64),
+        ("eps", ctypes.c_float),
     ]
 
 
@@ -159,6 +186,13 @@ def load() -> ctypes.CDLL:
         lib.qmm_linear_splitk_static.argtypes = [wp, vp, i64, ep, vp, i32, vp]
         lib.qmm_static_scratch_bytes.restype = ctypes.c_uint64
         lib.qmm_static_scratch_bytes.argtypes = []
+        tpp, tpn = ctypes.POINTER(QmmTpPeers), ctypes.POINTER(QmmTpNorm)
+        lib.qmm_tp_signal_ready.restype = i32
+        lib.qmm_tp_signal_ready.argtypes = [tpp, vp]
+        lib.qmm_tp_reduce_norm_gather.restype = i32
+        lib.qmm_tp_reduce_norm_gather.argtypes = [tpp, ctypes.c_uint64, i64, i64, vp, tpn, i32, i32, vp]
+        lib.qmm_tp_wait_gathered.restype = i32
+        lib.qmm_tp_wait_gathered.argtypes = [tpp, ctypes.c_uint64, vp]
         lib.qmm_set_weights_immutable.restype = i32
         lib.qmm_set_weights_immutable.argtypes = [i32]
         lib.qmm_debug_gemm_stall.restype = i32

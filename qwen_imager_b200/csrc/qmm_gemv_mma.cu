@@ -54,6 +54,7 @@
 // dequantized to f32 as scale * q + offset, f32 accumulation); the products
 // x * (128 + q) are exact in f32.  Every wait is bounded (qmm_common.cuh).
 #include <algorithm>
+#include <cstdlib>
 
 #include "qmm_epilogue.cuh"
 #include "qmm_internal.h"
@@ -209,7 +210,7 @@ __device__ __forceinline__ void stage_x8(const uint16_t *x, uint32_t *xp, float 
 //   part   [2][ks][rb][m] f32                         partial sums per K slice (ks = 16 warps)
 //   bars   full[kMaxStages], empty[kMaxStages], pready[2], pfree[2]
 template <int BITS, int MT, int TPW, int CW>
-__global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(const Params p) {
+__global__ void __launch_bounds__(Warps<CW>::kThreads, CW == 8 ? 2 : 1) qmm_gemv_mma_kernel(const Params p) {
     // sum_j x_j q_j = D_u - kOff * X_u (see the header comment).
     constexpr float kOff = BITS == 4 ? 128.0f : 2176.0f;
     using W = Warps<CW>;
@@ -427,14 +428,29 @@ __global__ void __launch_bounds__(Warps<CW>::kThreads, 1) qmm_gemv_mma_kernel(co
 
 struct Plan {
     int rb, ks, tpw, cw, stages, quad_stride, stage_bytes, meta_off, xp_stride;
+    int ctas_per_sm;  // 1: 16 consumer warps and the whole shared memory; 2: two CTAs of 8 warps per SM
     size_t smem;
 };
+
+// Two CTAs per SM (8 consumer warps, 16-row blocks, half the shared memory
+// each): twice the copy producers per SM, and the next launch's CTAs can
+// stream next to the previous launch's last ones.  QMM_GEMV_CTAS=1 or 2
+// overrides the choice (read once).
+static int gemv_ctas_choice() {
+    static const int v = [] {
+        const char *e = getenv("QMM_GEMV_CTAS");
+        return (e && (e[0] == '1' || e[0] == '2') && e[1] == '\0') ? e[0] - '0' : 0;
+    }();
+    return v;
+}
 
 // Units are 64 nibbles: 64 codes at 4 bits, 32 codes at 8 bits.
 static int64_t units_of(const qmm_weight &w) { return w.k * w.bits / 4 / kUnit; }
 
-static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
-    pl.cw = 16;
+static bool plan_for_ctas(const qmm_weight &w, int64_t m, int ctas, Plan &pl) {
+    pl.cw = ctas == 2 ? 8 : 16;
+    pl.ctas_per_sm = ctas;
+    const size_t limit = ctas == 2 ? (size_t)(227 * 1024) / 2 - 1024 : kSmemLimit;
     const int mt = m <= 8 ? 1 : 2;
     const int64_t units = units_of(w), groups = w.k / w.group;
     const int64_t row_bytes = w.k * w.bits / 8;
@@ -444,9 +460,10 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
     pl.xp_stride = (int)(units * 32 + 4);  // +16 bytes: tokens start in different bank quads
     const size_t xs = (size_t)(m + 1) * pl.xp_stride * 4 + (size_t)units * 8 * mt * 4;
     // A 32-row block (two tiles per warp) when three ring stages fit, else a
-    // 16-row block; with neither, any that fits two stages.
+    // 16-row block; with neither, any that fits two stages.  Two CTAs per SM
+    // use 16-row blocks.
     for (int pass = 0; pass < 2; ++pass)
-    for (int rb = 32; rb >= 16; rb /= 2) {
+    for (int rb = ctas == 2 ? 16 : 32; rb >= 16; rb /= 2) {
         // 16 warps on a 32-row block: one tile group of two tiles; otherwise
         // one tile per warp and rb / 16 tile groups.
         const int tpw = (pl.cw == 16 && rb == 32) ? 2 : 1;
@@ -455,7 +472,7 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
         const int64_t stage = (int64_t)(rb / 4) * pl.quad_stride + 2 * meta;
         const size_t fixed = xs + 2 * (size_t)ks * rb * m * 4 + 16 + (2 * kMaxStages + 4) * 8 + 64;
         int stages = kMaxStages;
-        while (stages >= 2 && fixed + (size_t)stages * stage > kSmemLimit) --stages;
+        while (stages >= 2 && fixed + (size_t)stages * stage > limit) --stages;
         if (stages < (pass == 0 ? 3 : 2)) continue;
         pl.rb = rb;
         pl.ks = ks;
@@ -467,6 +484,15 @@ static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
         return true;
     }
     return false;
+}
+
+static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
+    const int choice = gemv_ctas_choice();
+    if (choice == 2 || choice == 0) {
+        if (plan_for_ctas(w, m, 2, pl)) return true;
+        if (choice == 2) return false;
+    }
+    return plan_for_ctas(w, m, 1, pl);
 }
 
 template <int BITS, int MT, int TPW, int CW>
@@ -513,7 +539,7 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m, co
     p.err = device_error_word();
     const bool pdl = gemv_pdl_enabled();
     p.prefetch_weights = (pdl && weights_immutable()) ? 1 : 0;
-    const int grid = (int)std::min<int64_t>(p.nblocks, sm_count());
+    const int grid = (int)std::min<int64_t>(p.nblocks, (int64_t)sm_count() * pl.ctas_per_sm);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(Warps<CW>::kThreads);
@@ -549,6 +575,11 @@ qmm_status launch_gemv_mma(const qmm_weight &w, const uint16_t *x, int64_t m, co
                            uint16_t *y, cudaStream_t st) {
     gemvtc::Plan pl;
     if (!gemvtc::plan_for(w, m, pl)) return fail(QMM_ERR_UNSUPPORTED, "gemv (mma): layout does not fit shared memory");
+    if (pl.cw == 8) {  // two CTAs per SM: 16-row blocks, one tile per warp
+        if (w.bits == 8)
+            return m <= 8 ? gemvtc::launch_t<8, 1, 1, 8>(w, x, m, ep, y, st) : gemvtc::launch_t<8, 2, 1, 8>(w, x, m, ep, y, st);
+        return m <= 8 ? gemvtc::launch_t<4, 1, 1, 8>(w, x, m, ep, y, st) : gemvtc::launch_t<4, 2, 1, 8>(w, x, m, ep, y, st);
+    }
     if (w.bits == 8) {
         if (m <= 8)
             return pl.tpw == 2 ? gemvtc::launch_t<8, 1, 2, 16>(w, x, m, ep, y, st) : gemvtc::launch_t<8, 1, 1, 16>(w, x, m, ep, y, st);

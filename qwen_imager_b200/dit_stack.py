@@ -46,6 +46,7 @@ with the residual fused into the GEMM epilogue.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
@@ -293,12 +294,17 @@ class TensorParallel:
     collective's kernels have SMs to run on."""
 
     def __init__(self, rank: int = 0, world: int = 1, group=None, overlap_chunks: int = 1, comm_sms: int = 16,
-                 sequence_parallel: bool = True, sp_chunks: int = 1):
+                 sequence_parallel: bool = True, sp_chunks: int = 1, peer: bool = False):
         self.rank, self.world, self.group = rank, world, group
         self.overlap_chunks = overlap_chunks if world > 1 else 1
         self.comm_sms = comm_sms
         self.sequence_parallel = sequence_parallel and world > 1
         self.sp_chunks = sp_chunks if self.sequence_parallel else 1
+        # Sequence-parallel collectives over peer memory (qmm_tp_*), fused
+        # with the residual update and norm, instead of NCCL.
+        self.peer = peer and self.sequence_parallel
+        if self.peer and self.sp_chunks != 1:
+            raise ValueError("the peer-memory collectives run the stack in one token chunk")
 
     @classmethod
     def from_env(cls, **kw):
@@ -352,6 +358,62 @@ class TensorParallel:
         return None
 
 
+class PeerBuffers:
+    """The symmetric buffers of the peer-memory collectives (include/qmm.h,
+    qmm_tp_*): every rank's `part` (gated row-parallel partials), `gathered`
+    (normalised input of the column-parallel linears) and counters, mapped
+    into every rank's address space by torch's symmetric memory (allocation
+    and address exchange only; the data moves in this library's kernels)."""
+
+    def __init__(self, tokens: int, hidden: int, tp: "TensorParallel", device):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        group = tp.group or dist.group.WORLD
+        name = group.group_name
+        symm.enable_symm_mem_for_group(name)
+        self.part = symm.empty((tokens, hidden), dtype=torch.bfloat16, device=device)
+        self.gathered = symm.empty((tokens, hidden), dtype=torch.bfloat16, device=device)
+        self.counters = symm.empty((4,), dtype=torch.int64, device=device)
+        self.counters.zero_()
+        handles = [symm.rendezvous(t, name) for t in (self.part, self.gathered, self.counters)]
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every rank's counters are zero before anyone signals
+        self.peers = _lib.QmmTpPeers()
+        self.peers.world, self.peers.rank = tp.world, tp.rank
+        for j in range(tp.world):
+            self.peers.part[j] = handles[0].buffer_ptrs[j]
+            self.peers.gathered[j] = handles[1].buffer_ptrs[j]
+            self.peers.counters[j] = handles[2].buffer_ptrs[j]
+        self._handles = handles
+        self.epoch = 0  # qmm_tp_reduce_norm_gather calls so far (the same on every rank)
+
+    def exchange(self, x_local: torch.Tensor, split: int, vectors, reduce: bool, normalize: bool) -> None:
+        """One layer: this rank's partial is complete; reduce, update x_local,
+        normalise and gather; wait until every rank is done.  `vectors` holds
+        (bias, gate, shift, scale) per stream (entries may be None)."""
+        lib = _lib.load()
+        st = _stream_handle(x_local.device)
+        self.epoch += 1
+        norm = _lib.QmmTpNorm()
+        for s in range(2):
+            bias, gate, shift, scale = vectors[s]
+            if bias is None:
+                gate = None
+            norm.bias[s] = None if bias is None else bias.data_ptr()
+            norm.gate[s] = None if gate is None else gate.data_ptr()
+            norm.shift[s] = None if shift is None else shift.data_ptr()
+            norm.scale[s] = None if scale is None else scale.data_ptr()
+        norm.split = split
+        norm.eps = 1e-6
+        rows, hidden = x_local.shape
+        _lib.check(lib.qmm_tp_signal_ready(ctypes.byref(self.peers), st))
+        _lib.check(lib.qmm_tp_reduce_norm_gather(ctypes.byref(self.peers), self.epoch, rows, hidden,
+                                                  x_local.data_ptr(), ctypes.byref(norm), int(reduce),
+                                                  int(normalize), st))
+        _lib.check(lib.qmm_tp_wait_gathered(ctypes.byref(self.peers), self.epoch, st))
+
+
 class DitStack:
     """The 60-block dual-stream linear stack on one rank of a TP group."""
 
@@ -364,6 +426,7 @@ class DitStack:
         self.run_linear = run_linear
         self.attention = attention or _sdpa
         self._bufs = None
+        self._peer = None
 
     @classmethod
     def random(cls, cfg: StackConfig, tp: TensorParallel, seed: int = 0, device="cuda", blocks=None):
@@ -440,6 +503,8 @@ class DitStack:
         prev = lib.qmm_set_weights_immutable(1) if lib else 0
         try:
             mods = self.modulations(temb, timers)
+            if self.tp.peer and x.device.type == "cuda":
+                return self._forward_peer(x, mods, timers)
             if self.tp.sequence_parallel:
                 return self._forward_sequence_parallel(x, mods, timers)
             return self._forward_replicated(x, mods, timers)
@@ -559,6 +624,57 @@ class DitStack:
         with timers.span("comm"):
             for c in range(nc):
                 tp.all_gather(x[chunk[c]], xl[own[c]])
+        return x
+
+    def _forward_peer(self, x, mods, timers):
+        """Sequence-parallel form with the collectives over peer memory: per
+        row-parallel layer one qmm_tp_* exchange sums the ranks' partials of
+        this rank's tokens in f32, updates the residual, normalises for the
+        next linear and stores the result into every rank's gathered input."""
+        cfg, tp = self.cfg, self.tp
+        bufs = self._bufs[1]
+        if self._peer is None:
+            self._peer = PeerBuffers(cfg.tokens, cfg.hidden, tp, x.device)
+        pb = self._peer
+        part, nfull = pb.part, pb.gathered
+        qkv, attn, hid, xl = bufs["qkv"], bufs["attn"], bufs["hid"], bufs["xl"]
+        local = cfg.tokens // tp.world
+        lo = tp.rank * local
+        split = min(max(cfg.img_tokens - lo, 0), local)
+        rows = (slice(0, cfg.img_tokens), slice(cfg.img_tokens, cfg.tokens))
+        dl = cfg.heads * cfg.head_dim // tp.world
+        xl.copy_(x[lo:lo + local])
+        with timers.span("comm"):
+            pb.exchange(xl, split, [(None, None, mods[0, s, 0], mods[0, s, 1]) for s in range(2)],
+                        reduce=False, normalize=True)
+        nb = len(self.blocks)
+        for b, blk in enumerate(self.blocks):
+            m = mods[b]
+            with timers.span("linear"):
+                for s in range(2):
+                    self.run_linear(blk[s].qkv, nfull[rows[s]], out=qkv[rows[s]])
+            with timers.span("attention"):
+                self.attention(qkv, attn, dl // cfg.head_dim, cfg.head_dim)
+            with timers.span("linear"):
+                for s in range(2):
+                    self.run_linear(blk[s].out, attn[rows[s]], gate=m[s, 2], bias=None, out=part[rows[s]])
+            with timers.span("comm"):
+                pb.exchange(xl, split, [(blk[s].out_bias, m[s, 2], m[s, 3], m[s, 4]) for s in range(2)],
+                            reduce=True, normalize=True)
+            with timers.span("linear"):
+                for s in range(2):
+                    self.run_linear(blk[s].up, nfull[rows[s]], activation="gelu_tanh", out=hid[rows[s]])
+                for s in range(2):
+                    self.run_linear(blk[s].down, hid[rows[s]], gate=m[s, 5], bias=None, out=part[rows[s]])
+            last = b + 1 == nb
+            with timers.span("comm"):
+                if last:
+                    vec = [(blk[s].down_bias, m[s, 5], None, None) for s in range(2)]
+                else:
+                    vec = [(blk[s].down_bias, m[s, 5], mods[b + 1, s, 0], mods[b + 1, s, 1]) for s in range(2)]
+                pb.exchange(xl, split, vec, reduce=True, normalize=not last)
+        with timers.span("comm"):
+            tp.all_gather(x, xl)
         return x
 
     def _forward_replicated(self, x, mods, timers):

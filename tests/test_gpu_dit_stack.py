@@ -1,6 +1,7 @@
 """The tensor-parallel DiT linear stack on B200: CUDA linears against the
-oracle's linears on CPU, and (with two GPUs) NCCL tensor parallelism against
-one rank."""
+oracle's linears on CPU, and (with 2, 4 or 8 GPUs) tensor parallelism against
+one rank: NCCL collectives (sequence-parallel, chunked, replicated) and the
+library's peer-memory collectives (qmm_tp_*)."""
 import socket
 
 import pytest
@@ -50,7 +51,7 @@ def test_stack_cuda_matches_oracle_stack(cfg):
     assert mx <= 1e-2 and mean <= 1e-3, (mx, mean)
 
 
-def _nccl_rank(rank, world, port, seed, path, sp, chunks=1):
+def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
     import datetime
 
     import torch.distributed as dist
@@ -61,7 +62,7 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1):
         x, temb = _inputs(SMALL_TP, seed)
         dev = torch.device("cuda", rank)
         stack = DitStack.from_full(SMALL_TP, _weights(SMALL_TP, seed, dev),
-                                   TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks))
+                                   TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks, peer=peer))
         y = stack.forward(x.to(dev), temb.to(dev))
         torch.cuda.synchronize()
         torch.save(y.cpu(), f"{path}.{rank}")
@@ -72,10 +73,12 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1):
 
 # Sequence-parallel TP-N meets the one-rank bar; the replicated form sums the
 # whole hidden state in bf16 (see tests/test_dit_stack.py) and gets twice it.
-@pytest.mark.parametrize("world,sp,chunks", [(2, True, 1), (4, True, 1), (8, True, 1), (2, False, 1),
-                                              (2, True, 2), (8, True, 2)],
-                         ids=["sp2", "sp4", "sp8", "replicated2", "sp2-chunked", "sp8-chunked"])
-def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks):
+@pytest.mark.parametrize("world,sp,chunks,peer", [(2, True, 1, False), (4, True, 1, False), (8, True, 1, False),
+                                                   (2, False, 1, False), (2, True, 2, False), (8, True, 2, False),
+                                                   (2, True, 1, True), (4, True, 1, True), (8, True, 1, True)],
+                         ids=["sp2", "sp4", "sp8", "replicated2", "sp2-chunked", "sp8-chunked",
+                              "sp2-peer", "sp4-peer", "sp8-peer"])
+def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks, peer):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     seed = 23
@@ -86,7 +89,8 @@ def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     path = str(tmp_path / "y")
-    mp.start_processes(_nccl_rank, args=(world, port, seed, path, sp, chunks), nprocs=world, start_method="spawn")
+    mp.start_processes(_nccl_rank, args=(world, port, seed, path, sp, chunks, peer), nprocs=world,
+                       start_method="spawn")
     bar = 1e-2 if sp else 2e-2
     for r in range(world):
         mx, mean = rel_errors(_bits16(torch.load(f"{path}.{r}")), ref.float().cpu().numpy())

@@ -15,7 +15,9 @@ CRATE = os.path.join(ROOT, "qmm-sys", "src", "lib.rs")
 
 SCALARS = {"int64_t": "i64", "int32_t": "i32", "uint64_t": "u64", "uint32_t": "u32", "uint16_t": "u16",
            "float": "f32", "void": "c_void", "char": "c_char", "qmm_status": "qmm_status",
-           "qmm_weight": "qmm_weight", "qmm_epilogue": "qmm_epilogue"}
+           "qmm_weight": "qmm_weight", "qmm_epilogue": "qmm_epilogue", "qmm_tp_peers": "qmm_tp_peers",
+           "qmm_tp_norm": "qmm_tp_norm"}
+ARRAY_LENGTHS = {"QMM_TP_MAX_RANKS": 8}
 
 
 def _strip_c_comments(text):
@@ -37,6 +39,11 @@ def _c_type(t):
 
 def _c_param(p):
     p = " ".join(p.split())
+    arr = re.match(r"(.*?)(\w+)\s*\[(\w+)\]$", p)
+    if arr:  # a fixed-size array field: [T; N] in Rust
+        n = arr.group(3)
+        n = ARRAY_LENGTHS.get(n, n)
+        return arr.group(2), f"[{_c_type(arr.group(1))}; {n}]"
     m = re.match(r"(.*?)(\w+)$", p)
     return m.group(2), _c_type(m.group(1))
 
@@ -74,12 +81,10 @@ def crate_api():
                 params.append((n.strip(), _rust_type(t)))
         funcs[name] = (params, _rust_type(ret) if ret else "c_void")
     structs = {}
-    for name, body in re.findall(r"pub struct (\w+) \{(.*?)\}", text, re.S):
+    for name, body in re.findall(r"pub struct (\w+) \{(.*?)\n\}", text, re.S):
         fields = []
-        for f in body.split(","):
-            if f.strip():
-                n, t = f.replace("pub ", "").split(":", 1)
-                fields.append((n.strip(), _rust_type(t)))
+        for f in re.findall(r"pub (\w+): ([^\n]+?),\s*$", body, re.M):
+            fields.append((f[0], _rust_type(f[1])))
         structs[name] = fields
     consts = {k: int(v, 0) for k, v in re.findall(r"pub const (QMM_\w+): \w+ = (0x[0-9a-fA-F]+|\d+);", text)}
     return funcs, structs, consts
@@ -99,7 +104,7 @@ def test_every_header_function_is_bound_with_the_same_signature():
 def test_structs_have_the_same_layout():
     _, hs, _ = header_api()
     _, rs, _ = crate_api()
-    assert sorted(hs) == sorted(rs) == ["qmm_epilogue", "qmm_weight"]
+    assert sorted(hs) == sorted(rs) == ["qmm_epilogue", "qmm_tp_norm", "qmm_tp_peers", "qmm_weight"]
     for name, fields in hs.items():
         assert rs[name] == fields, name
 
