@@ -108,7 +108,11 @@ typedef enum qmm_path {
     QMM_PATH_GEMV = 1,   /* streaming GEMVs: tensor-core (4-bit, m <= 16), FMA (m <= 16),
                             warp-per-row (any m, slow for large m), first that fits */
     QMM_PATH_GEMM = 2,   /* tcgen05/TMEM GEMM, any m >= 1 */
-    QMM_PATH_GEMM_PAIR = 3  /* the GEMM on CTA pairs (cta_group::2, MMA M = 256) */
+    QMM_PATH_GEMM_PAIR = 3, /* the GEMM on CTA pairs (cta_group::2, MMA M = 256) */
+    QMM_PATH_GEMM_F16 = 4   /* the GEMM with fp16 operands: x is fp16 (not bf16) and the
+                               dequantized weights are rounded to fp16 (11 significant bits
+                               instead of bf16's 8; closer to the reference's f32 weights,
+                               src/quant.rs:105-113); y and the epilogue operands stay bf16 */
 } qmm_path;
 
 /* ABI version of the loaded library (QMM_ABI_VERSION at build time). */

@@ -51,6 +51,8 @@ pub const QMM_PATH_AUTO: qmm_path = 0;
 pub const QMM_PATH_GEMV: qmm_path = 1;
 pub const QMM_PATH_GEMM: qmm_path = 2;
 pub const QMM_PATH_GEMM_PAIR: qmm_path = 3;
+/// The GEMM with fp16 operands (x fp16, weights rounded to fp16); y stays bf16.
+pub const QMM_PATH_GEMM_F16: qmm_path = 4;
 
 /// A packed quantized weight: the `Affine` state of src/quant.rs:31-39.
 #[repr(C)]

@@ -43,6 +43,7 @@ QMM_PATH_AUTO = 0
 QMM_PATH_GEMV = 1
 QMM_PATH_GEMM = 2
 QMM_PATH_GEMM_PAIR = 3
+QMM_PATH_GEMM_F16 = 4
 
 QMM_EPILOGUE_RESIDUAL_MUL = 0x100
 

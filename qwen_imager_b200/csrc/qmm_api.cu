@@ -212,7 +212,7 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
     if (m < 0) return fail(QMM_ERR_BAD_SHAPE, "negative token count %lld", (long long)m);
     if (m == 0) return QMM_OK;
     if (!x || !y) return fail(QMM_ERR_INVALID_ARGUMENT, "null x or y");
-    if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM_PAIR)
+    if (path < QMM_PATH_AUTO || path > QMM_PATH_GEMM_F16)
         return fail(QMM_ERR_INVALID_ARGUMENT, "unknown path %d", path);
     qmm_epilogue e = ep ? *ep : qmm_epilogue{nullptr, nullptr, nullptr, QMM_ACT_NONE};
     if (!valid_activation(e.activation))
@@ -245,7 +245,7 @@ qmm_status qmm_linear_ex(const qmm_weight *w, const uint16_t *x, int64_t m,
                     "gemm: %d-bit, group %d, k=%lld is outside the kernel's layouts (needs 4/8-bit, "
                     "k %% 64 == 0, group 32 or a multiple of 64)",
                     w->bits, w->group, (long long)w->k);
-    return qmm::launch_gemm(*w, x, m, e, y, path == QMM_PATH_GEMM_PAIR, 1, nullptr, st);
+    return qmm::launch_gemm(*w, x, m, e, y, path == QMM_PATH_GEMM_PAIR, 1, nullptr, st, path == QMM_PATH_GEMM_F16);
 }
 
 int32_t qmm_gemm_splits(const qmm_weight *w, int64_t m) {

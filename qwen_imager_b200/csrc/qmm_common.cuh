@@ -448,6 +448,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
            | ((m >> 4) << 24);   // M / 16
 }
 
+// Instruction descriptor for kind::f16 with fp16 A and B, f32 accumulator,
+// both operands K-major, shape M x N (A and B formats 0 = f16).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
+    return (1u << 4)             // accumulator format: f32
+           | ((n >> 3) << 17)    // N / 8
+           | ((m >> 4) << 24);   // M / 16
+}
+
 // ---------------------------------------------------------------- numerics
 __device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

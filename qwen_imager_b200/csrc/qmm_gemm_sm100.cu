@@ -60,7 +60,7 @@ struct Warps {
 // T: tokens per tile (MMA N, accumulator columns).  PAIR: the tile spans a CTA
 // pair (cta_group::2, MMA M = 256), each CTA holding 128 weight rows and T/2
 // of the tile's tokens in shared memory.
-template <int BITS, int T, bool PAIR>
+template <int BITS, int T, bool PAIR, bool F16 = false>
 struct Cfg {
     static_assert(T % 32 == 0 && T >= 32 && T <= 256, "token tile");
     static constexpr int kXRows = PAIR ? T / 2 : T;                // x rows staged per CTA
@@ -88,7 +88,8 @@ struct Cfg {
     static_assert(2 * T + kASlots * 32 <= kTmemCols, "TMEM budget");
     static_assert(kXStageBytes % 1024 == 0 && kPStageBytes % 1024 == 0, "stage alignment");
     static_assert(kSmemBytes <= 232448, "shared memory");
-    static constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * kWRows : kWRows, T);
+    static constexpr uint32_t kIdesc = F16 ? idesc_f16_f32(PAIR ? 2 * kWRows : kWRows, T)
+                                           : idesc_bf16_f32(PAIR ? 2 * kWRows : kWRows, T);
 };
 
 // Work unit u of num_units = tiles * splits covers output tile u % tiles and
@@ -137,7 +138,7 @@ __device__ __forceinline__ uint32_t packed_chunk_offset(int r, int c) {
 // m0 / m1 = scale | offset << 16 (bf16 bits) of the groups holding codes
 // [0, 32) and [32, 64) of the block (equal unless group == 32).  NH halves
 // starting at half H0 (or at `hbase` when H0 < 0) are produced.
-template <int BITS, int H0, int NH>
+template <int BITS, int H0, int NH, bool F16 = false>
 __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m0, uint32_t m1, int row,
                                                   uint32_t (&a)[16 * NH], int hbase) {
 #pragma unroll
@@ -153,7 +154,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 uint32_t o4[4];
-                dequant_word_bf16x2_packed<4>(ws[j], sc, of, o4);
+                dequant_word_bf16x2_packed<4, F16>(ws[j], sc, of, o4);
 #pragma unroll
                 for (int t = 0; t < 4; ++t) a[hh * 16 + j * 4 + t] = o4[t];
             }
@@ -165,7 +166,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint32_t o2[2];
-                    dequant_word_bf16x2_packed<8>(ws[j], sc, of, o2);
+                    dequant_word_bf16x2_packed<8, F16>(ws[j], sc, of, o2);
                     a[hh * 16 + cc * 8 + j * 2 + 0] = o2[0];
                     a[hh * 16 + cc * 8 + j * 2 + 1] = o2[1];
                 }
@@ -174,7 +175,7 @@ __device__ __forceinline__ void dequant_row_block(const uint8_t *pst, uint32_t m
     }
 }
 
-template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false>
+template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false, bool F16 = false>
 __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
     qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w,
@@ -495,8 +496,8 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
             const uint8_t *pst = smem + C::kPOff + s * C::kPStageBytes;
             constexpr int kV = HALVES == 1 ? 32 : 16;
             uint32_t v[kV];
-            if constexpr (HALVES == 1) dequant_row_block<BITS, 0, 2>(pst, m0, m1, row, v, 0);
-            else dequant_row_block<BITS, -1, 1>(pst, m0, m0, row, v, half);
+            if constexpr (HALVES == 1) dequant_row_block<BITS, 0, 2, F16>(pst, m0, m1, row, v, 0);
+            else dequant_row_block<BITS, -1, 1, F16>(pst, m0, m0, row, v, half);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[s]);  // the stage's codes are in registers
             const int ab = p.kpair ? (a >> 1) : a;  // the slot's barrier (shared by a slot pair)
@@ -761,11 +762,11 @@ static qmm_status make_map_3d_f32(CUtensorMap *map, const void *base, uint64_t i
     return QMM_OK;
 }
 
-template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false>
+template <int BITS, int T, int SETS, int HALVES, bool PAIR, bool STALL = false, bool F16 = false>
 static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
                            const qmm_epilogue &ep, uint16_t *y, int splits, float *ws, cudaStream_t st) {
-    using C = Cfg<BITS, T, PAIR>;
-    auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR, STALL>;
+    using C = Cfg<BITS, T, PAIR, F16>;
+    auto kernel = qmm_gemm_kernel<BITS, T, SETS, HALVES, PAIR, STALL, F16>;
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -777,7 +778,8 @@ static qmm_status launch_t(const qmm_weight &w, const uint16_t *x, int64_t m,
         configured[dev] = true;
     }
     CUtensorMap tx, tw;
-    qmm_status s = make_map_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)w.k,
+    qmm_status s = make_map_2d(&tx, F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                               x, (uint64_t)w.k,
                                (uint64_t)m, (uint64_t)w.k * 2, kBK, C::kXRows,
                                CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != QMM_OK) return s;
@@ -901,8 +903,13 @@ int gemm_recommended_splits(const qmm_weight &w, int64_t m) {
 }
 
 qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
-                       uint16_t *y, bool pair, int splits, float *ws, cudaStream_t st) {
+                       uint16_t *y, bool pair, int splits, float *ws, cudaStream_t st, bool f16) {
     if (m > (int64_t)INT32_MAX - 256) return fail(QMM_ERR_UNSUPPORTED, "gemm: m too large");
+    if (f16) {
+        // fp16 operands: x in fp16, the dequantized weights rounded to fp16.
+        return w.bits == 4 ? gemm::launch_t<4, 192, 4, 1, false, false, true>(w, x, m, ep, y, splits, ws, st)
+                           : gemm::launch_t<8, 192, 4, 1, false, false, true>(w, x, m, ep, y, splits, ws, st);
+    }
     // Token tile 192 (two 192-column accumulators + four A slots fill TMEM);
     // four dequantization warp sets of full rows.  CTA pairs (cta_group::2)
     // on request: they halve the x traffic per SM but lengthen the A-slot

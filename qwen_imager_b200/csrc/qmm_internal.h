@@ -59,7 +59,8 @@ bool gemm_supported(const qmm_weight &w);
 // Split-K factor worth using for this shape (1 = none).
 int gemm_recommended_splits(const qmm_weight &w, int64_t m);
 // splits > 1: ws holds splits * m * n floats (16-byte aligned); k / 64 % splits == 0; n % 4 == 0.
+// f16: x is fp16 and the weights are dequantized to fp16 (QMM_PATH_GEMM_F16).
 qmm_status launch_gemm(const qmm_weight &w, const uint16_t *x, int64_t m, const qmm_epilogue &ep,
-                       uint16_t *y, bool pair, int splits, float *ws, cudaStream_t st);
+                       uint16_t *y, bool pair, int splits, float *ws, cudaStream_t st, bool f16 = false);
 
 }  // namespace qmm

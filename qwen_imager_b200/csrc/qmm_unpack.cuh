@@ -9,6 +9,8 @@
 // permute plus one exact subtraction turns a code into a float.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "qmm_common.cuh"
 
 namespace qmm {
@@ -101,7 +103,9 @@ __device__ __forceinline__ uint32_t magic_byte_bits(uint32_t v) {
     return __byte_perm(v, 0x4B000000u, 0x7440u + I);
 }
 
-template <int BITS>
+// F16: the same values rounded to fp16 pairs instead (the GEMM's fp16-operand
+// instantiation; 11 significant bits instead of 8).
+template <int BITS, bool F16 = false>
 __device__ __forceinline__ void dequant_word_bf16x2_packed(uint32_t w, float2 s2, float2 o2,
                                                            uint32_t (&out)[WordCodes<BITS>::kCount / 2]) {
     constexpr int C = WordCodes<BITS>::kCount;
@@ -130,7 +134,12 @@ __device__ __forceinline__ void dequant_word_bf16x2_packed(uint32_t w, float2 s2
         const float2 f = make_float2(__uint_as_float(m[2 * i]), __uint_as_float(m[2 * i + 1]));
         const float2 q = add_f32x2(f, neg_magic);
         const float2 v = fma_f32x2(q, s2, o2);
-        out[i] = pack_bf16x2_rn(v.x, v.y);
+        if constexpr (F16) {
+            const __half2 h = __floats2half2_rn(v.x, v.y);
+            out[i] = *reinterpret_cast<const uint32_t *>(&h);
+        } else {
+            out[i] = pack_bf16x2_rn(v.x, v.y);
+        }
     }
 }
 

@@ -133,6 +133,8 @@ class Affine:
         w = self.c_weight()
         lib = _lib.load()
         gemm = path == _lib.QMM_PATH_GEMM or (path == _lib.QMM_PATH_AUTO and m > 16)
+        if path == _lib.QMM_PATH_GEMM_F16:
+            gemm, splits = False, 1  # one launch of the fp16-operand GEMM (no split-K)
         if gemm and m > 0:
             sp = lib.qmm_gemm_splits(ctypes.byref(w), m) if splits is None else int(splits)
             if sp > 1:
@@ -241,17 +243,22 @@ class Linear:
                       residual: Optional[torch.Tensor] = None,
                       activation: Optional[str] = None, path: int = _lib.QMM_PATH_AUTO,
                       out: Optional[torch.Tensor] = None, splits: Optional[int] = None,
-                      bias=OWN_BIAS, residual_mul: bool = False) -> torch.Tensor:
+                      bias=OWN_BIAS, residual_mul: bool = False, operands: str = "bf16") -> torch.Tensor:
         """residual + gate * act(x . W^T + bias) with any leading dims on x.
 
         gate: [output] per-feature multiplier; residual: same shape as the output;
         bias: replaces the layer's own bias (None: no bias); residual_mul: the
         residual multiplies instead, residual * (gate * act(x . W^T + bias)).
 
-        bf16 inputs run the fused kernels.  f32 inputs take the reference's
-        non-fused route (src/quant.rs:121): the weight dequantized to f32
-        (bit-exact) and a dense f32 GEMM, with an f32 result.
+        bf16 inputs run the fused kernels.  operands="fp16" (or an fp16 x) runs
+        the GEMM with fp16 operands (QMM_PATH_GEMM_F16): x converted to fp16,
+        the weights dequantized to fp16, closer to the reference's f32 weights;
+        the result stays bf16.  f32 inputs take the reference's non-fused route
+        (src/quant.rs:121): the weight dequantized to f32 (bit-exact) and a
+        dense f32 GEMM, with an f32 result.
         """
+        if operands not in ("bf16", "fp16"):
+            raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT, f"operands must be bf16 or fp16, not {operands!r}")
         if activation not in ACTIVATIONS:
             raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT, f"unknown activation {activation!r}")
         *lead, k = x.shape
@@ -274,7 +281,13 @@ class Linear:
                 out.view(m, a.output).copy_(t)
                 return out
             return t.reshape(*lead, a.output)
-        if x.dtype != torch.bfloat16:
+        if x.dtype == torch.float16 or operands == "fp16":
+            if x.dtype not in (torch.bfloat16, torch.float16):
+                raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT, f"fp16 operands from a {x.dtype} input")
+            x = x.to(torch.float16)
+            path = _lib.QMM_PATH_GEMM_F16
+            splits = 1
+        elif x.dtype != torch.bfloat16:
             raise QmmError(_lib.QMM_ERR_INVALID_ARGUMENT,
                            f"quantized linear computes in bf16 (or f32 through dequantization); got {x.dtype}")
         x2d = x.reshape(m, k)
