@@ -433,9 +433,10 @@ struct Plan {
 };
 
 // Two CTAs per SM (8 consumer warps, 16-row blocks, half the shared memory
-// each): twice the copy producers per SM, and the next launch's CTAs can
-// stream next to the previous launch's last ones.  QMM_GEMV_CTAS=1 or 2
-// overrides the choice (read once).
+// each): twice the copy producers per SM, and the next launch's CTAs could
+// stream next to the previous launch's last ones.  Measured slower than one
+// CTA of 16 warps (adaLN 1 x 3072 x 18432: 11.65 vs 10.47 us at 4-bit, 22.79
+// vs 18.50 us at 8-bit), so it runs only with QMM_GEMV_CTAS=2 (read once).
 static int gemv_ctas_choice() {
     static const int v = [] {
         const char *e = getenv("QMM_GEMV_CTAS");
@@ -487,11 +488,7 @@ static bool plan_for_ctas(const qmm_weight &w, int64_t m, int ctas, Plan &pl) {
 }
 
 static bool plan_for(const qmm_weight &w, int64_t m, Plan &pl) {
-    const int choice = gemv_ctas_choice();
-    if (choice == 2 || choice == 0) {
-        if (plan_for_ctas(w, m, 2, pl)) return true;
-        if (choice == 2) return false;
-    }
+    if (gemv_ctas_choice() == 2) return plan_for_ctas(w, m, 2, pl);
     return plan_for_ctas(w, m, 1, pl);
 }
 

@@ -29,8 +29,12 @@
 // on every rank waits for count >= k * world.  Every wait is bounded
 // (%globaltimer); on expiry the kernel records an error in the library's
 // device error word (qmm_device_error) and skips its work, so every rank's
-// next wait expires too instead of hanging.  No multicast and no TMA: plain
-// 16-byte peer loads and stores.
+// next wait expires too instead of hanging.  The reduction streams the
+// partials with bulk copies (cp.async.bulk, no multicast) from every rank's
+// memory into a shared-memory ring (reduce_pipelined_kernel); the normalised
+// rows go out with plain 16-byte stores.
+#include <algorithm>
+
 #include "qmm_epilogue.cuh"
 #include "qmm_internal.h"
 
@@ -55,6 +59,7 @@ struct Args {
     const uint16_t *bias[2], *gate[2], *shift[2], *scale[2];
     float eps;
     uint32_t *err;
+    int32_t stages;       // pipelined kernel: shared-memory ring stages (a power of two, 2..16)
 };
 
 __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t *p) {
@@ -92,9 +97,17 @@ __global__ void signal_ready_kernel(Args a) {
     for (int j = 0; j < a.world; ++j) red_add_release_sys(a.counters[j] + kReady, 1);
 }
 
-// One thread: wait until every rank has stored its normalised rows here.
+// Orders this thread's generic-proxy accesses (the acquire of a counter)
+// before its later async-proxy accesses of global memory (bulk copies, TMA).
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// One thread: wait until every rank has stored its normalised rows here (the
+// next kernel reads them, also through TMA).
 __global__ void wait_done_kernel(Args a) {
     wait_counter(a.counters[a.rank] + kDone, a.epoch * (uint64_t)a.world, a.err);
+    fence_proxy_async_global();
 }
 
 template <int VPL, bool REDUCE, bool NORM>
@@ -221,6 +234,195 @@ __global__ void __launch_bounds__(kWarps * 32) reduce_norm_gather_kernel(Args a)
     }
 }
 
+// The residual update and norm of one row, and the stores of the normalised
+// row into every rank's `gathered`, from the row's f32 sum of partials
+// `acc` (lane's elements, VPL groups of 8).
+template <int VPL, bool NORM>
+__device__ __forceinline__ void finish_row(const Args &a, int64_t row, int lane, float (&acc)[VPL][8]) {
+    constexpr int H = VPL * 8 * 32;
+    const int s = row >= a.split ? 1 : 0;
+    const int64_t grow = (int64_t)a.rank * a.rows + row;
+    uint4 *xr = reinterpret_cast<uint4 *>(a.x + row * H);
+    const uint4 *b4 = reinterpret_cast<const uint4 *>(a.bias[s]);
+    const uint4 *g4 = reinterpret_cast<const uint4 *>(a.gate[s]);
+    uint32_t xv[VPL][4];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const uint4 v = xr[i * 32 + lane];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint4 bv = make_uint4(0, 0, 0, 0), gv = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+        if (b4) bv = __ldg(b4 + i * 32 + lane);
+        if (b4 && g4) gv = __ldg(g4 + i * 32 + lane);
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float lo = __uint_as_float(w[q] << 16) + acc[i][2 * q];
+            float hi = __uint_as_float(w[q] & 0xFFFF0000u) + acc[i][2 * q + 1];
+            lo += __uint_as_float(bw[q] << 16) * __uint_as_float(gw[q] << 16);
+            hi += __uint_as_float(bw[q] & 0xFFFF0000u) * __uint_as_float(gw[q] & 0xFFFF0000u);
+            xv[i][q] = pack_bf16x2_rn(lo, hi);
+        }
+        xr[i * 32 + lane] = make_uint4(xv[i][0], xv[i][1], xv[i][2], xv[i][3]);
+    }
+    if constexpr (NORM) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sum += __uint_as_float(xv[i][q] << 16) + __uint_as_float(xv[i][q] & 0xFFFF0000u);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        const float mean = sum * (1.0f / H);
+        float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float lo = __uint_as_float(xv[i][q] << 16) - mean;
+                const float hi = __uint_as_float(xv[i][q] & 0xFFFF0000u) - mean;
+                sq = fmaf(lo, lo, fmaf(hi, hi, sq));
+            }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        const float rstd = rsqrtf(sq * (1.0f / H) + a.eps);
+        const uint4 *sh4 = reinterpret_cast<const uint4 *>(a.shift[s]);
+        const uint4 *sc4 = reinterpret_cast<const uint4 *>(a.scale[s]);
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            const uint4 c4 = __ldg(sc4 + i * 32 + lane), h4 = __ldg(sh4 + i * 32 + lane);
+            const uint32_t cw[4] = {c4.x, c4.y, c4.z, c4.w}, hw[4] = {h4.x, h4.y, h4.z, h4.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float lo = (__uint_as_float(xv[i][q] << 16) - mean) * rstd;
+                const float hi = (__uint_as_float(xv[i][q] & 0xFFFF0000u) - mean) * rstd;
+                o[q] = pack_bf16x2_rn(fmaf(lo, 1.0f + __uint_as_float(cw[q] << 16), __uint_as_float(hw[q] << 16)),
+                                      fmaf(hi, 1.0f + __uint_as_float(cw[q] & 0xFFFF0000u),
+                                           __uint_as_float(hw[q] & 0xFFFF0000u)));
+            }
+            const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+            for (int j = 0; j < a.world; ++j)
+                reinterpret_cast<uint4 *>(a.gathered[j] + grow * H)[i * 32 + lane] = ov;
+        }
+    }
+}
+
+// Pipelined reduce (+ norm + gather): a persistent grid of one CTA per SM.
+// Warp 0's lane 0 bulk-copies, for each row this CTA owns (rows c, c + grid,
+// ...), the row's slice of every rank's `part` into one stage of a shared-
+// memory ring (world * hidden * 2 bytes per stage; copies from peer memory,
+// no multicast).  Consumer warp w (of NW) takes the CTA's rows i with
+// i % NW == w; stage = i % stages, and stages is a multiple of NW, so each
+// stage has one consumer, which takes its phases in order.  The ring keeps
+// up to ~190 KB per SM in flight over NVLink, where register loads kept a
+// quarter of that.
+template <int VPL, bool NORM>
+__global__ void __launch_bounds__(32 * 9, 1) reduce_pipelined_kernel(Args a) {
+    constexpr int H = VPL * 8 * 32;
+    constexpr int kRowBytes = H * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = a.stages;
+    const int NW = S < 8 ? S : 8;  // consumer warps
+    const uint32_t stage_bytes = (uint32_t)a.world * kRowBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * stage_bytes);
+    uint64_t *empty = full + S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int64_t nrows = a.rows <= blockIdx.x ? 0 : (a.rows - 1 - blockIdx.x) / gridDim.x + 1;  // this CTA's rows
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            bool ok = wait_counter(a.counters[a.rank] + kReady, a.epoch * (uint64_t)a.world, a.err);
+            fence_proxy_async_global();  // the bulk copies below read what the acquire made visible
+            int64_t i = 0;
+            for (; ok && i < nrows; ++i) {
+                const int s = (int)(i % S);
+                if (i >= S && !mbar_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1), a.err, kErrTimeoutPeer)) {
+                    ok = false;
+                    break;
+                }
+                const int64_t grow = (int64_t)a.rank * a.rows + (int64_t)blockIdx.x + i * gridDim.x;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                uint8_t *dst = smem + (size_t)s * stage_bytes;
+                for (int j = 0; j < a.world; ++j)
+                    bulk_load(dst + (size_t)j * kRowBytes, a.part[j] + grow * H, kRowBytes, &full[s]);
+            }
+            // Let the copies issued land before the CTA exits (the consumers
+            // wait for every stage they take; after an error, wait here).
+            if (!ok)
+                for (int64_t k = i > S ? i - S : 0; k < i; ++k)
+                    mbar_wait(&full[k % S], (uint32_t)((k / S) & 1), a.err, kErrTimeoutPeer);
+        }
+    } else if (warp - 1 < NW) {
+        // ------------------------------------------------------------ consumers
+        const int c = warp - 1;
+        bool ok = true;
+        for (int64_t i = c; ok && i < nrows; i += NW) {
+            const int s = (int)(i % S);
+            ok = mbar_wait(&full[s], (uint32_t)((i / S) & 1), a.err, kErrTimeoutPeer);
+            if (!ok) break;
+            const uint8_t *st = smem + (size_t)s * stage_bytes;
+            float acc[VPL][8];
+#pragma unroll
+            for (int v = 0; v < VPL; ++v)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[v][e] = 0.0f;
+            for (int j = 0; j < a.world; ++j) {
+                const uint4 *pr = reinterpret_cast<const uint4 *>(st + (size_t)j * kRowBytes);
+#pragma unroll
+                for (int v = 0; v < VPL; ++v) {
+                    const uint4 u = pr[v * 32 + lane];
+                    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        acc[v][2 * q] += __uint_as_float(w[q] << 16);
+                        acc[v][2 * q + 1] += __uint_as_float(w[q] & 0xFFFF0000u);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // the stage's data is in registers
+            finish_row<VPL, NORM>(a, (int64_t)blockIdx.x + i * gridDim.x, lane, acc);
+        }
+    }
+    // Done: as in reduce_norm_gather_kernel.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        uint64_t *local = a.counters[a.rank] + kLocal;
+        const unsigned long long old = atomicAdd(reinterpret_cast<unsigned long long *>(local), 1ull);
+        if (old + 1 == gridDim.x) {
+            *local = 0;
+            __threadfence_system();
+            for (int j = 0; j < a.world; ++j) red_add_release_sys(a.counters[j] + kDone, 1);
+        }
+    }
+}
+
+template <int VPL>
+static qmm_status launch_pipelined(cudaStream_t st, Args &a, bool norm) {
+    const size_t stage = (size_t)a.world * VPL * 8 * 32 * 2;
+    constexpr size_t kBudget = 200 * 1024;
+    int S = 16;
+    while (S > 2 && (size_t)S * stage > kBudget) S >>= 1;
+    if ((size_t)S * stage > kBudget) return fail(QMM_ERR_UNSUPPORTED, "tp: a row of every rank does not fit the ring");
+    a.stages = S;
+    const size_t smem = (size_t)S * stage + 2 * (size_t)S * 8;
+    auto kernel = norm ? reduce_pipelined_kernel<VPL, true> : reduce_pipelined_kernel<VPL, false>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "tp smem attribute");
+    const unsigned grid = (unsigned)std::min<int64_t>(a.rows, sm_count());
+    kernel<<<grid, 32 * 9, smem, st>>>(a);
+    return QMM_OK;
+}
+
 template <int VPL>
 static void launch_rng(unsigned grid, cudaStream_t st, const Args &a, bool reduce, bool norm) {
     const int kT = kWarps * 32;
@@ -316,14 +518,27 @@ qmm_status qmm_tp_reduce_norm_gather(const qmm_tp_peers *peers, uint64_t epoch, 
     a.eps = nrm->eps;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = (unsigned)((rows + qmm::tp::kWarps - 1) / qmm::tp::kWarps);
-    switch ((int)(hidden / 256) * (hidden % 256 == 0 ? 1 : 0)) {
-        case 1: qmm::tp::launch_rng<1>(grid, st, a, reduce, normalize); break;
-        case 2: qmm::tp::launch_rng<2>(grid, st, a, reduce, normalize); break;
-        case 4: qmm::tp::launch_rng<4>(grid, st, a, reduce, normalize); break;
-        case 12: qmm::tp::launch_rng<12>(grid, st, a, reduce, normalize); break;
-        case 16: qmm::tp::launch_rng<16>(grid, st, a, reduce, normalize); break;
-        default:
-            return fail(QMM_ERR_UNSUPPORTED, "tp: hidden %lld is not 256, 512, 1024, 3072 or 4096", (long long)hidden);
+    const int vpl = (int)(hidden / 256) * (hidden % 256 == 0 ? 1 : 0);
+    if (vpl != 1 && vpl != 2 && vpl != 4 && vpl != 12 && vpl != 16)
+        return fail(QMM_ERR_UNSUPPORTED, "tp: hidden %lld is not 256, 512, 1024, 3072 or 4096", (long long)hidden);
+    if (reduce) {
+        // The reduction streams every rank's rows through the pipelined kernel.
+        switch (vpl) {
+            case 1: s = qmm::tp::launch_pipelined<1>(st, a, normalize); break;
+            case 2: s = qmm::tp::launch_pipelined<2>(st, a, normalize); break;
+            case 4: s = qmm::tp::launch_pipelined<4>(st, a, normalize); break;
+            case 12: s = qmm::tp::launch_pipelined<12>(st, a, normalize); break;
+            default: s = qmm::tp::launch_pipelined<16>(st, a, normalize); break;
+        }
+        if (s != QMM_OK) return s;
+    } else {
+        switch (vpl) {
+            case 1: qmm::tp::launch_rng<1>(grid, st, a, reduce, normalize); break;
+            case 2: qmm::tp::launch_rng<2>(grid, st, a, reduce, normalize); break;
+            case 4: qmm::tp::launch_rng<4>(grid, st, a, reduce, normalize); break;
+            case 12: qmm::tp::launch_rng<12>(grid, st, a, reduce, normalize); break;
+            default: qmm::tp::launch_rng<16>(grid, st, a, reduce, normalize); break;
+        }
     }
     qmm::count_launch();
     cudaError_t e = cudaGetLastError();
