@@ -84,8 +84,9 @@ def parse():
     p.add_argument("--sp-chunks", type=int, default=1,
                    help="dit_* on N > 1: token chunks whose reduce-scatter / all-gather overlap the other chunks' "
                         "linears (1 = none)")
-    p.add_argument("--peer", action="store_true",
-                   help="dit_* on N > 1: the sequence-parallel collectives over peer memory (qmm_tp_*) instead of NCCL")
+    p.add_argument("--comm", choices=["peer", "nccl"], default="peer",
+                   help="dit_* on N > 1, one token chunk, sequence-parallel: the per-layer reduce + norm + gather "
+                        "over peer memory (qmm_tp_*, the default) or as NCCL reduce-scatter / all-gather")
     p.add_argument("--comm-sms", type=int, default=16,
                    help="dit_* with --sp-chunks > 1: SMs the GEMMs leave to the collectives")
     a = p.parse_args()
@@ -94,6 +95,8 @@ def parse():
         a.steps = 10 if stack else 300
     if a.warmup is None:
         a.warmup = 3 if stack else 5
+    # The peer-memory exchange serves the one-chunk sequence-parallel form.
+    a.peer = a.comm == "peer" and not a.replicated and a.sp_chunks == 1
     return a
 
 
@@ -899,14 +902,20 @@ def main():
 def main_stack(args, world, rank, local):
     from qwen_imager_b200.dit_stack import STACKS
     cfg = STACKS[args.workload]
-    form = ("replicated hidden state, NCCL all-reduce after each row-parallel layer" if args.replicated else
-            "sequence-parallel: NCCL reduce-scatter after each row-parallel layer, fused residual + LayerNorm + "
-            "modulation on the local tokens, NCCL all-gather before each column-parallel layer")
+    if args.replicated:
+        form = "replicated hidden state, NCCL all-reduce after each row-parallel layer"
+    elif args.peer:
+        form = ("sequence-parallel over peer memory: after each row-parallel layer one qmm_tp_* exchange sums "
+                "the ranks' partials of the local tokens in f32, applies residual + LayerNorm + modulation and "
+                "writes the result into every rank's input buffer")
+    else:
+        form = ("sequence-parallel: NCCL reduce-scatter after each row-parallel layer, fused residual + LayerNorm + "
+                "modulation on the local tokens, NCCL all-gather before each column-parallel layer")
     config = {"workload": f"{args.workload}: {STACK_WORKLOADS[args.workload]}", "global_batch": 1,
               "tokens": cfg.tokens, "hidden": cfg.hidden, "blocks": cfg.blocks, "bits": cfg.bits, "group": cfg.group,
               "parallelism": f"tp{world} (column-parallel QKV/up/modulation, row-parallel out/down; {form})"
                              if world > 1 else "tp1",
-              "overlap_chunks": args.overlap_chunks, "sp_chunks": args.sp_chunks, "peer_collectives": args.peer,
+              "overlap_chunks": args.overlap_chunks, "sp_chunks": args.sp_chunks, "peer_collectives": args.peer and world > 1,
               "l2": "weights of every step (GBs) far exceed L2 (no flush); per-layer timings walk over the blocks' "
                     "weights (inputs + weights of each launch > 126 MB)"}
     common = {"metric": STACK_METRIC, "unit": "ms", "steps": args.steps, "warmup": args.warmup,

@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(Warps<SETS, HALVES>::kThreads, 1)
                     const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_out,
                     const __grid_constant__ CUtensorMap tmap_res, const Params p) {
-    using C = Cfg<BITS, T, PAIR>;
+    using C = Cfg<BITS, T, PAIR, F16>;
     using W = Warps<SETS, HALVES>;
     // The normal instantiation waits with the constant limit and withholds
     // nothing (the same code as without test support).

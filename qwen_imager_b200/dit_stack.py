@@ -48,6 +48,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
 
@@ -369,6 +370,9 @@ class PeerBuffers:
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
 
+        # The kernels use plain peer loads and stores: ask torch not to bind
+        # the buffers to an NVLink multicast object.
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         group = tp.group or dist.group.WORLD
         name = group.group_name
         symm.enable_symm_mem_for_group(name)
