@@ -76,6 +76,8 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(STACK_WORKLOADS), default="dit_2048_8bit")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-configs", action="store_true",
+                   help="dit_* on one GPU: skip timing the single-linear configurations beside the stack")
     p.add_argument("--no-parity", action="store_true", help="dit_*: skip the untimed TP-vs-one-rank check (N > 1)")
     p.add_argument("--replicated", action="store_true",
                    help="dit_*: all-reduce the whole hidden state on every rank instead of the sequence-parallel form")
@@ -497,6 +499,61 @@ def time_stack_layers(stack, cfg, world, steps, device):
     return results
 
 
+# The single-linear configurations also timed inside the stack line at N = 1
+# (each on its own 20-launch graph, rotating over weight sets larger than L2).
+CONFIG_LINES = (("config1 linear_4bit", "linear_4bit"), ("config2 ffn_up", "ffn_up"),
+                ("config3 ffn_down", "ffn_down"), ("adaln_gemv_8bit", "adaln_gemv_8bit"))
+
+
+def time_configs(device, steps=20):
+    """Per-launch device time of the single-linear configurations (GEMMs and
+    the modulation GEMV) with their rooflines against the burst peaks: the
+    region of each is a few milliseconds."""
+    import torch
+
+    burst_tf, _, hbm_gbs, _ = measured_peaks()
+    out = []
+    cap = torch.cuda.Stream(device)
+    for label, name in CONFIG_LINES:
+        _, layers, seed = WORKLOADS[name]
+        sets = build_sets(layers, seed, device)
+        for li, (m, k, n, bits, ex) in enumerate(layers):
+            rot = sets[li]
+
+            def launch(i, rot=rot, ex=ex):
+                lin, x, res, y = rot[i % len(rot)]
+                lin.forward_fused(x, residual=res, out=y, activation=ex.get("activation"))
+
+            for i in range(3):
+                launch(i)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(cap):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    for i in range(steps):
+                        launch(i)
+            torch.cuda.synchronize()
+            g.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) / steps * 1e3
+            e = {"config": label, "m": m, "k": k, "n": n, "bits": bits, "kernel_us": round(us, 2)}
+            if m <= 16:
+                gbs = (n * k * bits / 8 + n * (k // 64) * 4 + m * k * 2 + m * n * 2) / (us * 1e-6) / 1e9
+                e.update({"GB/s": round(gbs, 1), "hbm_frac": round(gbs / hbm_gbs, 4)})
+            else:
+                tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+                e.update({"TFLOP/s": round(tf, 1), "frac_of_burst": round(tf / burst_tf, 4)})
+            out.append(e)
+            del g
+        del sets
+        torch.cuda.empty_cache()
+    return out
+
+
 def choose_peak(region_s, clocks):
     """Burst or sustained bf16 denominator for a kernel timed in a region of
     `region_s` seconds with clock record `clocks`: sustained only when the
@@ -690,11 +747,14 @@ def run_stack(args, rank, world, device):
         "linear_tflops_per_rank": round(lin_flops / world / (lin_ms * 1e-3) / 1e12, 1) if lin_ms else None,
         "attention_tflops_per_rank": round(att_flops / world / (parts.get("attention", float("nan")) * 1e-3) / 1e12, 1),
         "linear_tflop_per_step": round(lin_flops / 1e12, 2), "attention_tflop_per_step": round(att_flops / 1e12, 2),
-        "collectives_per_step": (4 * cfg.blocks + 1 if tp.sequence_parallel else 2 * cfg.blocks) + (1 if dist else 0),
+        "collectives_per_step": ((2 * cfg.blocks + 2 if tp.peer else
+                                  4 * cfg.blocks + 1 if tp.sequence_parallel else 2 * cfg.blocks)
+                                 + (1 if dist else 0)),
     })
+    configs = time_configs(device) if (world == 1 and not args.no_configs) else None
     return {"value": round(ms, 3), "ms_per_step": round(ms, 3), "e2e": e2e, "roofline": roof,
             "gpu_launches": int(launches), "breakdown": breakdown, "clocks": clocks, "layers": layers,
-            "tp_parity": parity, "form": "sequence-parallel" if tp.sequence_parallel else
+            "configs": configs, "tp_parity": parity, "form": "sequence-parallel" if tp.sequence_parallel else
             ("replicated" if dist else "one rank")}
 
 
@@ -951,6 +1011,8 @@ def main_stack(args, world, rank, local):
                    e2e=res["e2e"], roofline=res["roofline"], gpu_launches=res["gpu_launches"],
                    clocks=res["clocks"], breakdown=res["breakdown"], layers=res["layers"],
                    tp_parity=res["tp_parity"])
+        if res["configs"] is not None:
+            out["configs"] = res["configs"]
         if rank == 0 and world == 1 and not args.no_cpu:
             try:
                 ms, cores, sample, _ = cpu_stack_reference(args.workload, len(STACK_PIECES))
