@@ -554,6 +554,48 @@ def time_configs(device, steps=20):
     return out
 
 
+PEER_COPY_GBS = 770.0  # measured peer-copy bandwidth per direction per B200 on this NVSwitch fabric
+
+
+def time_exchange(stack, cfg, world, rank, device, reps=20):
+    """Device time of the peer-memory exchange alone: every rank enters
+    together (barrier, 3 untimed exchanges), then `reps` exchanges back to
+    back, max over ranks.  Per exchange each rank reads the other ranks'
+    partials of its tokens and stores its normalised tokens into the other
+    ranks' buffers: (world - 1) * (tokens / world) * hidden * 2 bytes over
+    NVLink in each direction, the roofline's numerator."""
+    import torch
+    import torch.distributed as tdist
+
+    pb = stack._peer
+    xl = stack._bufs[1]["xl"]
+    local = cfg.tokens // world
+    lo = rank * local
+    split = min(max(cfg.img_tokens - lo, 0), local)
+    z = torch.zeros((cfg.hidden,), dtype=torch.bfloat16, device=device)
+    vec = [(z, z, z, z), (z, z, z, z)]
+    for _ in range(3):
+        pb.exchange(xl, split, vec, reduce=True, normalize=True)
+    torch.cuda.synchronize()
+    tdist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        pb.exchange(xl, split, vec, reduce=True, normalize=True)
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / reps], device=device, dtype=torch.float64)
+    tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+    us = float(t.item()) * 1e3
+    remote = (world - 1) * local * cfg.hidden * 2
+    gbs = remote / (us * 1e-6) / 1e9
+    return {"us_per_exchange": round(us, 2), "nvlink_bytes_per_direction": int(remote),
+            "achieved_gbs_per_direction": round(gbs, 1), "peak_gbs_per_direction": PEER_COPY_GBS,
+            "frac": round(gbs / PEER_COPY_GBS, 4),
+            "what": "qmm_tp_signal_ready + qmm_tp_reduce_norm_gather + qmm_tp_wait_gathered on zeroed "
+                    f"vectors, {reps} back to back after a barrier, max over ranks; peak = measured peer copy"}
+
+
 def choose_peak(region_s, clocks):
     """Burst or sustained bf16 denominator for a kernel timed in a region of
     `region_s` seconds with clock record `clocks`: sustained only when the
@@ -737,6 +779,7 @@ def run_stack(args, rank, world, device):
                "d2h_bytes_per_step": int(hy.numel() * 2),
                "what": "the public DitStack.forward with the hidden state and timestep copied in from pinned host "
                        "memory and the new hidden state read back, every step (bytes per rank)"}
+    exchange = time_exchange(stack, cfg, world, rank, device) if (dist and tp.peer) else None
     if device_error(device):
         raise RuntimeError("device-side wait expired during the timed region")
     parity = (tp_parity(cfg.bits, rank, world, device, args.sp_chunks, args.peer)
@@ -754,7 +797,7 @@ def run_stack(args, rank, world, device):
     configs = time_configs(device) if (world == 1 and not args.no_configs) else None
     return {"value": round(ms, 3), "ms_per_step": round(ms, 3), "e2e": e2e, "roofline": roof,
             "gpu_launches": int(launches), "breakdown": breakdown, "clocks": clocks, "layers": layers,
-            "configs": configs, "tp_parity": parity, "form": "sequence-parallel" if tp.sequence_parallel else
+            "configs": configs, "exchange": exchange, "tp_parity": parity, "form": "sequence-parallel" if tp.sequence_parallel else
             ("replicated" if dist else "one rank")}
 
 
@@ -1013,6 +1056,8 @@ def main_stack(args, world, rank, local):
                    tp_parity=res["tp_parity"])
         if res["configs"] is not None:
             out["configs"] = res["configs"]
+        if res["exchange"] is not None:
+            out["exchange"] = res["exchange"]
         if rank == 0 and world == 1 and not args.no_cpu:
             try:
                 ms, cores, sample, _ = cpu_stack_reference(args.workload, len(STACK_PIECES))
