@@ -200,5 +200,7 @@ def test_argument_errors_are_reported():
     assert lib.qmm_linear_ex(ctypes.byref(w), x.data_ptr(), 4, None, y.data_ptr(), 9, None) == _lib.QMM_ERR_INVALID_ARGUMENT
     with pytest.raises(_lib.QmmError):
         lin.forward(torch.zeros((4, 100), dtype=torch.bfloat16, device="cuda"))
-    with pytest.raises(_lib.QmmError):  # f16 activations: neither the bf16 kernels nor the f32 route
-        lin.forward(torch.zeros((4, 128), dtype=torch.float16, device="cuda"))
+    with pytest.raises(_lib.QmmError):  # f64 activations: no kernel and no dense route serves them
+        lin.forward(torch.zeros((4, 128), dtype=torch.float64, device="cuda"))
+    # f16 activations run the GEMM with fp16 operands (tests/test_gpu_f16_operands.py).
+    assert lin.forward(torch.zeros((4, 128), dtype=torch.float16, device="cuda")).dtype == torch.bfloat16
