@@ -558,12 +558,15 @@ PEER_COPY_GBS = 770.0  # measured peer-copy bandwidth per direction per B200 on 
 
 
 def time_exchange(stack, cfg, world, rank, device, reps=20):
-    """Device time of the peer-memory exchange alone: every rank enters
-    together (barrier, 3 untimed exchanges), then `reps` exchanges back to
-    back, max over ranks.  Per exchange each rank reads the other ranks'
-    partials of its tokens and stores its normalised tokens into the other
-    ranks' buffers: (world - 1) * (tokens / world) * hidden * 2 bytes over
-    NVLink in each direction, the roofline's numerator."""
+    """Device time of the peer-memory exchange alone: 3 untimed exchanges, a
+    barrier, one more untimed exchange enqueued right before the start event
+    (it ends on every rank only when every rank has finished it, so the ranks'
+    timed regions start together on the device, whatever the host skew after
+    the barrier), then `reps` exchanges back to back, max over ranks.  Per
+    exchange each GPU's NVLink carries, in each direction, the partials it
+    serves to the other ranks plus the normalised rows it stores into them:
+    2 * (world - 1) * (tokens / world) * hidden * 2 bytes, the roofline's
+    numerator."""
     import torch
     import torch.distributed as tdist
 
@@ -578,6 +581,7 @@ def time_exchange(stack, cfg, world, rank, device, reps=20):
         pb.exchange(xl, split, vec, reduce=True, normalize=True)
     torch.cuda.synchronize()
     tdist.barrier()
+    pb.exchange(xl, split, vec, reduce=True, normalize=True)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(reps):
@@ -587,13 +591,14 @@ def time_exchange(stack, cfg, world, rank, device, reps=20):
     t = torch.tensor([a.elapsed_time(b) / reps], device=device, dtype=torch.float64)
     tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
     us = float(t.item()) * 1e3
-    remote = (world - 1) * local * cfg.hidden * 2
+    remote = 2 * (world - 1) * local * cfg.hidden * 2
     gbs = remote / (us * 1e-6) / 1e9
     return {"us_per_exchange": round(us, 2), "nvlink_bytes_per_direction": int(remote),
             "achieved_gbs_per_direction": round(gbs, 1), "peak_gbs_per_direction": PEER_COPY_GBS,
             "frac": round(gbs / PEER_COPY_GBS, 4),
             "what": "qmm_tp_signal_ready + qmm_tp_reduce_norm_gather + qmm_tp_wait_gathered on zeroed "
-                    f"vectors, {reps} back to back after a barrier, max over ranks; peak = measured peer copy"}
+                    f"vectors, {reps} back to back after an aligning exchange, max over ranks; bytes = partials "
+                    "served + rows stored per GPU per direction; peak = measured peer copy per direction"}
 
 
 def choose_peak(region_s, clocks):

@@ -250,6 +250,13 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void 
                  "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
                  : "memory");
 }
+// Contiguous shared -> global bulk copy (size and both addresses 16-byte
+// aligned), completion tracked per thread in bulk groups.
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's bulk groups beyond the newest N have finished reading shared memory.
 template <int N>

@@ -34,6 +34,7 @@
 // memory into a shared-memory ring (reduce_pipelined_kernel); the normalised
 // rows go out with plain 16-byte stores.
 #include <algorithm>
+#include <cstdlib>
 
 #include "qmm_epilogue.cuh"
 #include "qmm_internal.h"
@@ -236,9 +237,11 @@ __global__ void __launch_bounds__(kWarps * 32) reduce_norm_gather_kernel(Args a)
 
 // The residual update and norm of one row, and the stores of the normalised
 // row into every rank's `gathered`, from the row's f32 sum of partials
-// `acc` (lane's elements, VPL groups of 8).
-template <int VPL, bool NORM>
-__device__ __forceinline__ void finish_row(const Args &a, int64_t row, int lane, float (&acc)[VPL][8]) {
+// `acc` (lane's elements, VPL groups of 8).  BULK: the normalised row goes to
+// the warp's shared-memory row `out` instead, for the caller's bulk stores.
+template <int VPL, bool NORM, bool BULK = false>
+__device__ __forceinline__ void finish_row(const Args &a, int64_t row, int lane, float (&acc)[VPL][8],
+                                           uint4 *out = nullptr) {
     constexpr int H = VPL * 8 * 32;
     const int s = row >= a.split ? 1 : 0;
     const int64_t grow = (int64_t)a.rank * a.rows + row;
@@ -301,10 +304,20 @@ __device__ __forceinline__ void finish_row(const Args &a, int64_t row, int lane,
                                            __uint_as_float(hw[q] & 0xFFFF0000u)));
             }
             const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
-            for (int j = 0; j < a.world; ++j)
-                reinterpret_cast<uint4 *>(a.gathered[j] + grow * H)[i * 32 + lane] = ov;
+            if constexpr (BULK) {
+                out[i * 32 + lane] = ov;
+            } else {
+                for (int j = 0; j < a.world; ++j)
+                    reinterpret_cast<uint4 *>(a.gathered[j] + grow * H)[i * 32 + lane] = ov;
+            }
         }
     }
+}
+
+// Shared memory of the pipelined kernel: the ring (S stages of world rows),
+// its full / empty barriers, then (bulk stores) one output row per consumer warp.
+__host__ __device__ constexpr size_t out_offset(int S, size_t stage_bytes) {
+    return ((size_t)S * stage_bytes + 2 * (size_t)S * 8 + 127) & ~(size_t)127;
 }
 
 // Pipelined reduce (+ norm + gather): a persistent grid of one CTA per SM.
@@ -316,7 +329,13 @@ __device__ __forceinline__ void finish_row(const Args &a, int64_t row, int lane,
 // stage has one consumer, which takes its phases in order.  The ring keeps
 // up to ~190 KB per SM in flight over NVLink, where register loads kept a
 // quarter of that.
-template <int VPL, bool NORM>
+//
+// BULK (with NORM): each consumer warp writes its normalised row into its own
+// shared-memory row and lane 0 hands it to the copy engine as one bulk store
+// per rank (6 KB at hidden 3072) instead of every lane storing 16 bytes per
+// rank; the warp waits for those stores to have read the row before it
+// writes the next one, and for them to complete before the CTA signals.
+template <int VPL, bool NORM, bool BULK = false>
 __global__ void __launch_bounds__(32 * 9, 1) reduce_pipelined_kernel(Args a) {
     constexpr int H = VPL * 8 * 32;
     constexpr int kRowBytes = H * 2;
@@ -363,6 +382,10 @@ __global__ void __launch_bounds__(32 * 9, 1) reduce_pipelined_kernel(Args a) {
     } else if (warp - 1 < NW) {
         // ------------------------------------------------------------ consumers
         const int c = warp - 1;
+        constexpr bool kBulk = BULK && NORM;
+        uint4 *outb = nullptr;
+        if constexpr (kBulk)
+            outb = reinterpret_cast<uint4 *>(smem + out_offset(S, stage_bytes) + (size_t)c * kRowBytes);
         bool ok = true;
         for (int64_t i = c; ok && i < nrows; i += NW) {
             const int s = (int)(i % S);
@@ -389,7 +412,27 @@ __global__ void __launch_bounds__(32 * 9, 1) reduce_pipelined_kernel(Args a) {
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);  // the stage's data is in registers
-            finish_row<VPL, NORM>(a, (int64_t)blockIdx.x + i * gridDim.x, lane, acc);
+            const int64_t row = (int64_t)blockIdx.x + i * gridDim.x;
+            if constexpr (kBulk) {
+                if (lane == 0) bulk_wait_read<0>();  // the previous row's stores have read `outb`
+                __syncwarp();
+            }
+            finish_row<VPL, NORM, kBulk>(a, row, lane, acc, outb);
+            if constexpr (kBulk) {
+                fence_proxy_async_smem();  // this lane's row elements before the copy engine reads them
+                __syncwarp();
+                if (lane == 0) {
+                    const int64_t grow = (int64_t)a.rank * a.rows + row;
+                    for (int j = 0; j < a.world; ++j) bulk_store(a.gathered[j] + grow * H, outb, kRowBytes);
+                    bulk_commit();
+                }
+            }
+        }
+        if constexpr (kBulk) {
+            if (lane == 0) {
+                bulk_wait_all();             // the rows have landed in every rank's `gathered`
+                fence_proxy_async_global();  // before the generic-proxy release below
+            }
         }
     }
     // Done: as in reduce_norm_gather_kernel.
@@ -406,16 +449,47 @@ __global__ void __launch_bounds__(32 * 9, 1) reduce_pipelined_kernel(Args a) {
     }
 }
 
+// Bulk stores of the normalised rows (QMM_TP_BULK_STORE=1) instead of
+// per-lane stores.
+static bool bulk_store_rows() {
+    static const bool on = [] {
+        const char *e = std::getenv("QMM_TP_BULK_STORE");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 template <int VPL>
 static qmm_status launch_pipelined(cudaStream_t st, Args &a, bool norm) {
-    const size_t stage = (size_t)a.world * VPL * 8 * 32 * 2;
-    constexpr size_t kBudget = 200 * 1024;
-    int S = 16;
-    while (S > 2 && (size_t)S * stage > kBudget) S >>= 1;
-    if ((size_t)S * stage > kBudget) return fail(QMM_ERR_UNSUPPORTED, "tp: a row of every rank does not fit the ring");
+    const size_t row = (size_t)VPL * 8 * 32 * 2;
+    const size_t stage = (size_t)a.world * row;
+    const bool bulk = norm && bulk_store_rows();
+    int S = 0;
+    size_t smem = 0;
+    if (!bulk) {
+        constexpr size_t kBudget = 200 * 1024;
+        S = 16;
+        while (S > 2 && (size_t)S * stage > kBudget) S >>= 1;
+        if ((size_t)S * stage > kBudget) return fail(QMM_ERR_UNSUPPORTED, "tp: a row of every rank does not fit the ring");
+        smem = (size_t)S * stage + 2 * (size_t)S * 8;
+    } else {
+        // Ring plus one output row per consumer warp (min(S, 8) of them); S is
+        // at most 8 or 16 so that every stage has one consumer.
+        constexpr size_t kLimit = 225 * 1024;
+        static const int kCand[] = {16, 8, 7, 6, 5, 4, 3, 2};
+        for (int cand : kCand) {
+            const size_t need = out_offset(cand, stage) + (size_t)(cand < 8 ? cand : 8) * row;
+            if (need <= kLimit) {
+                S = cand;
+                smem = need;
+                break;
+            }
+        }
+        if (!S) return fail(QMM_ERR_UNSUPPORTED, "tp: two rows of every rank do not fit the ring");
+    }
     a.stages = S;
-    const size_t smem = (size_t)S * stage + 2 * (size_t)S * 8;
-    auto kernel = norm ? reduce_pipelined_kernel<VPL, true> : reduce_pipelined_kernel<VPL, false>;
+    auto kernel = !norm ? reduce_pipelined_kernel<VPL, false>
+                        : (bulk ? reduce_pipelined_kernel<VPL, true, true> : reduce_pipelined_kernel<VPL, true>);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "tp smem attribute");
     const unsigned grid = (unsigned)std::min<int64_t>(a.rows, sm_count());

@@ -2,6 +2,7 @@
 oracle's linears on CPU, and (with 2, 4 or 8 GPUs) tensor parallelism against
 one rank: NCCL collectives (sequence-parallel, chunked, replicated) and the
 library's peer-memory collectives (qmm_tp_*)."""
+import os
 import socket
 
 import pytest
@@ -55,6 +56,8 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
     import datetime
 
     import torch.distributed as dist
+    if peer == "bulk":  # the exchange's bulk-store variant, read once when the library first launches it
+        os.environ["QMM_TP_BULK_STORE"] = "1"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
@@ -62,7 +65,8 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
         x, temb = _inputs(SMALL_TP, seed)
         dev = torch.device("cuda", rank)
         stack = DitStack.from_full(SMALL_TP, _weights(SMALL_TP, seed, dev),
-                                   TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks, peer=peer))
+                                   TensorParallel(rank, world, sequence_parallel=sp, sp_chunks=chunks,
+                                                  peer=bool(peer)))
         y = stack.forward(x.to(dev), temb.to(dev))
         torch.cuda.synchronize()
         torch.save(y.cpu(), f"{path}.{rank}")
@@ -75,9 +79,10 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
 # whole hidden state in bf16 (see tests/test_dit_stack.py) and gets twice it.
 @pytest.mark.parametrize("world,sp,chunks,peer", [(2, True, 1, False), (4, True, 1, False), (8, True, 1, False),
                                                    (2, False, 1, False), (2, True, 2, False), (8, True, 2, False),
-                                                   (2, True, 1, True), (4, True, 1, True), (8, True, 1, True)],
+                                                   (2, True, 1, True), (4, True, 1, True), (8, True, 1, True),
+                                                   (2, True, 1, "bulk"), (8, True, 1, "bulk")],
                          ids=["sp2", "sp4", "sp8", "replicated2", "sp2-chunked", "sp8-chunked",
-                              "sp2-peer", "sp4-peer", "sp8-peer"])
+                              "sp2-peer", "sp4-peer", "sp8-peer", "sp2-peer-bulk", "sp8-peer-bulk"])
 def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks, peer):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
