@@ -56,8 +56,8 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
     import datetime
 
     import torch.distributed as dist
-    if peer == "bulk":  # the exchange's bulk-store variant, read once when the library first launches it
-        os.environ["QMM_TP_BULK_STORE"] = "1"
+    if peer == "lanes":  # the exchange's per-lane-store variant, read when the library first launches it
+        os.environ["QMM_TP_BULK_STORE"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
@@ -80,9 +80,9 @@ def _nccl_rank(rank, world, port, seed, path, sp, chunks=1, peer=False):
 @pytest.mark.parametrize("world,sp,chunks,peer", [(2, True, 1, False), (4, True, 1, False), (8, True, 1, False),
                                                    (2, False, 1, False), (2, True, 2, False), (8, True, 2, False),
                                                    (2, True, 1, True), (4, True, 1, True), (8, True, 1, True),
-                                                   (2, True, 1, "bulk"), (8, True, 1, "bulk")],
+                                                   (2, True, 1, "lanes"), (8, True, 1, "lanes")],
                          ids=["sp2", "sp4", "sp8", "replicated2", "sp2-chunked", "sp8-chunked",
-                              "sp2-peer", "sp4-peer", "sp8-peer", "sp2-peer-bulk", "sp8-peer-bulk"])
+                              "sp2-peer", "sp4-peer", "sp8-peer", "sp2-peer-lanes", "sp8-peer-lanes"])
 def test_stack_nccl_matches_one_rank(tmp_path, world, sp, chunks, peer):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
