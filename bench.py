@@ -56,6 +56,9 @@ WORKLOADS = {
     # The 2048x2048 stack's image-stream FFN-up GEMM on one rank (for profiles).
     "stack_img_up": ("image-stream FFN up 8-bit [16384x3072]x[12288x3072]^T + GELU-tanh",
                      [(16384, 3072, 12288, 8, {"activation": "gelu_tanh"})], 6),
+    # Its image-stream out-projection as one of 8 row-parallel shards (K = 3072 / 8).
+    "stack_out_shard8": ("image-stream out-projection shard of 8 ranks, 8-bit [16384x384]x[3072x384]^T",
+                         [(16384, 384, 3072, 8, {})], 7),
 }
 STACK_WORKLOADS = {
     "dit_1024_4bit": "60-block dual-stream DiT linear stack, 1024x1024 (4096 image + 256 text tokens), 4-bit",
