@@ -96,3 +96,49 @@ def test_one_rank_exchange_matches_f32_steps(rows, hidden, split):
         assert float(dg.max()) <= 2.0 ** -6 * max(1.0, float(want_g.float().abs().max())), (epoch, float(dg.max()))
         assert float(dg.mean()) <= 1e-3 * float(want_g.float().abs().mean()), epoch
     np.testing.assert_array_equal(counters[:2].cpu().numpy(), [2, 2])  # ready, done after two epochs
+
+
+@pytest.mark.gpu
+def test_a_rank_that_never_signals_is_reported_as_a_timeout():
+    """A two-rank group emulated in one process whose rank 1 never runs: rank
+    0's exchange waits for rank 1's ready signal (a counter nothing else will
+    raise), gives up after its bounded wait (4 s), skips its work and reports
+    QMM_ERR_TIMEOUT through qmm_device_error; the context stays usable, and a
+    one-rank exchange launched after it is correct."""
+    lib = _lib.load()
+    dev = torch.device("cuda")
+    rows, hidden = 64, 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    x = _bf16(torch.randn((rows, hidden), generator=g, device=dev))
+    x0 = x.clone()
+    part = [torch.zeros((2 * rows, hidden), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    gathered = [torch.zeros((2 * rows, hidden), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    counters = [torch.zeros((4,), dtype=torch.int64, device=dev) for _ in range(2)]
+    peers = _peers(world=2, rank=0)
+    for j in range(2):
+        peers.part[j], peers.gathered[j], peers.counters[j] = (part[j].data_ptr(), gathered[j].data_ptr(),
+                                                               counters[j].data_ptr())
+    ones = torch.ones((hidden,), dtype=torch.bfloat16, device=dev)
+    norm = _lib.QmmTpNorm()
+    for s in range(2):
+        norm.bias[s], norm.gate[s], norm.shift[s], norm.scale[s] = (ones.data_ptr(),) * 4
+    norm.split, norm.eps = rows // 2, 1e-6
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert device_error() == 0
+    import time
+    t0 = time.monotonic()
+    assert lib.qmm_tp_signal_ready(ctypes.byref(peers), st) == _lib.QMM_OK
+    assert lib.qmm_tp_reduce_norm_gather(ctypes.byref(peers), 1, rows, hidden, ctypes.c_void_p(x.data_ptr()),
+                                         ctypes.byref(norm), 1, 1, st) == _lib.QMM_OK
+    assert lib.qmm_tp_wait_gathered(ctypes.byref(peers), 1, st) == _lib.QMM_OK
+    torch.cuda.synchronize()
+    took = time.monotonic() - t0
+    code = ctypes.c_uint32()
+    assert lib.qmm_device_error(st, ctypes.byref(code)) == _lib.QMM_ERR_TIMEOUT
+    assert code.value != 0
+    assert 3.0 < took < 60.0, took
+    assert torch.equal(x, x0)  # the exchange skipped its work
+    assert not bool(gathered[0].any()) and not bool(gathered[1].any())
+    assert device_error() == 0  # reading the code cleared it
+    test_one_rank_exchange_matches_f32_steps(37, 256, 20)
